@@ -1,0 +1,238 @@
+/*
+ * mtr_sampler.h -- C ABI of the fused decode-sampling step (logits-processor
+ * chain + token sampler) for Mapperatorinator-style event-token decoders on
+ * NVIDIA B200 (sm_100a).
+ *
+ * One call processes B output rows of a [R, V] logits matrix (R = B, or 2B
+ * with classifier-free guidance) and, depending on `select_mode`, writes the
+ * processed scores, the greedy token or a token drawn from caller-supplied
+ * uniforms.  All buffers are caller-owned device memory; the library
+ * allocates nothing, never synchronises the stream and never throws.  Every
+ * entry point returns an MtrStatus code.
+ *
+ * Reference interfaces replaced (paths are inside the Mapperatorinator
+ * project; "HF:" means transformers/generation/ of the pinned transformers):
+ *   mtr_sampler_launch, select_mode = MTR_SELECT_NONE
+ *       replaces LogitsProcessorList.__call__ over the chain built by
+ *       build_logits_processor_list (osuT5/osuT5/inference/logit_processors.py:240-307)
+ *       -- ClassifierFreeGuidanceLogitsProcessor (HF:logits_process.py:2160-2174),
+ *       MonotonicTimeShiftLogitsProcessor (logit_processors.py:173-237),
+ *       TimeshiftBias (logit_processors.py:35-43),
+ *       ConditionalTemperatureLogitsWarper (logit_processors.py:46-119),
+ *       TemperatureLogitsWarper (HF:logits_process.py:297-301) -- followed by the
+ *       warpers generate() appends: TopKLogitsWarper (HF:logits_process.py:581-588)
+ *       and TopPLogitsWarper (HF:logits_process.py:521-535).
+ *   mtr_sampler_launch, select_mode = MTR_SELECT_ARGMAX / MTR_SELECT_SAMPLE
+ *       replaces _sample(logits, do_sample, top_p, top_k, temperature)
+ *       (osuT5/osuT5/inference/compiled_decode.py:1135-1158) and the
+ *       softmax + torch.multinomial / argmax block of the decode loops
+ *       (osuT5/osuT5/inference/optimized/single/decode_loop.py:289-301,
+ *       HF:utils.py:2762-2793), plus the pad-on-finished step
+ *       (decode_loop.py:303-305).
+ *   mono_state (MTR_MONO_STATE) replaces the per-row state of the stateful
+ *       monotonic processors (osuT5/osuT5/inference/optimized/single/logits.py:13-113,
+ *       compiled_decode.py:309-372).
+ */
+#ifndef MTR_SAMPLER_H
+#define MTR_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MTR_ABI_VERSION 1
+
+/* Limits (also reported by mtr_sampler_query). */
+#define MTR_MAX_VOCAB 131072
+#define MTR_MAX_IDS_LEN 65535
+#define MTR_MAX_SOS_IDS 16
+#define MTR_MAX_COND_TEMPS 4
+#define MTR_MAX_COL_TEMP_RANGES 8
+#define MTR_MAX_GRAMMAR_CLASSES 32
+#define MTR_MAX_EOS_IDS 16
+#define MTR_MAX_EOS_RANGES 2
+
+/* Return codes of every entry point. */
+typedef enum MtrStatus {
+  MTR_OK = 0,
+  MTR_ERR_NULL_ARG = 1,     /* a required pointer is NULL */
+  MTR_ERR_BAD_SHAPE = 2,    /* vocab / rows / strides / ids_len out of range */
+  MTR_ERR_BAD_PARAM = 3,    /* a scalar parameter out of its domain */
+  MTR_ERR_UNSUPPORTED = 4,  /* a valid request this build cannot serve */
+  MTR_ERR_ALIGNMENT = 5,    /* a pointer is not aligned to its element size */
+  MTR_ERR_CUDA = 6,         /* the CUDA runtime reported an error */
+  MTR_ERR_ABI = 7           /* abi_version / struct_size mismatch */
+} MtrStatus;
+
+/* Per-row status bits written to out_status (0 = clean row). */
+#define MTR_ROW_NONFINITE   (1u << 0) /* a processed score is NaN or +inf        */
+#define MTR_ROW_ALL_MASKED  (1u << 1) /* every processed score is -inf           */
+#define MTR_ROW_BAD_ID      (1u << 2) /* an input id outside [0, vocab) was skipped */
+#define MTR_ROW_BAD_UNIFORM (1u << 3) /* uniform outside [0, 1) was clamped      */
+#define MTR_ROW_SLOW_PATH   (1u << 4) /* exact radix fallback was used (info)     */
+#define MTR_ROW_TIE_AT_CUT  (1u << 5) /* the top-p cut split equal scores (info)  */
+
+typedef enum MtrDType { MTR_DTYPE_F32 = 0, MTR_DTYPE_BF16 = 1, MTR_DTYPE_F16 = 2 } MtrDType;
+typedef enum MtrIdType { MTR_IDS_I64 = 0, MTR_IDS_I32 = 1 } MtrIdType;
+
+typedef enum MtrMonoMode {
+  MTR_MONO_OFF = 0,
+  MTR_MONO_STATE = 1, /* mask from mono_state[row] (-1 = inactive, else last value) */
+  MTR_MONO_SCAN = 2   /* recompute the state from input_ids (full scan); stores it in
+                         mono_state when that pointer is set */
+} MtrMonoMode;
+
+typedef enum MtrTempMode {
+  MTR_TEMP_SCALAR = 0,          /* scores / temperature                                   */
+  MTR_TEMP_ROW_CONDITIONAL = 1, /* per-row temperature picked from input_ids (first match) */
+  MTR_TEMP_COLUMN_RANGES = 2    /* per-vocab-range temperature, `temperature` elsewhere    */
+} MtrTempMode;
+
+typedef enum MtrTopPMode {
+  MTR_TOPP_HF = 0,       /* keep token while mass ranked strictly above it <  top_p */
+  MTR_TOPP_SAMPLE_FN = 1 /* keep token while mass ranked strictly above it <= top_p */
+} MtrTopPMode;
+
+typedef enum MtrSelect {
+  MTR_SELECT_NONE = 0,   /* processor only: write out_scores / out_logprobs   */
+  MTR_SELECT_ARGMAX = 1, /* greedy: first index of the maximum (top-k/p unused) */
+  MTR_SELECT_SAMPLE = 2  /* inverse-CDF draw from uniforms[row]                  */
+} MtrSelect;
+
+/* flags */
+#define MTR_FLAG_MONO_UPDATE_FROM_IDS       (1u << 0) /* fold input_ids[:, -1] into mono_state before masking */
+#define MTR_FLAG_MONO_UPDATE_FROM_SAMPLE    (1u << 1) /* fold the emitted token into mono_state after the draw */
+#define MTR_FLAG_GRAMMAR_PREV_FROM_IDS      (1u << 2) /* previous token = input_ids[:, -1] instead of prev_token */
+#define MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE (1u << 3) /* prev_token[row] = emitted token after the draw        */
+#define MTR_FLAG_FORCE_RADIX                (1u << 4) /* test hook: always take the exact radix selection path  */
+
+/*
+ * All pointer fields are device pointers (host pointers for the CPU oracle
+ * that shares this struct).  Optional pointers may be NULL.  Initialise with
+ * mtr_args_init() and then set what is needed.
+ */
+typedef struct MtrSamplerArgs {
+  uint32_t abi_version; /* = MTR_ABI_VERSION */
+  uint32_t struct_size; /* = sizeof(MtrSamplerArgs) */
+
+  /* ---- logits [rows, vocab], row i and (with CFG) row i + cfg_second_offset ---- */
+  const void* logits;
+  int64_t logits_row_stride; /* elements */
+  int64_t cfg_second_offset; /* rows; <= 0 means num_rows */
+  int32_t logits_dtype;      /* MtrDType */
+  int32_t num_rows;          /* B = output rows */
+  int32_t vocab;             /* V */
+  int32_t cfg_enabled;       /* out = second + (first - second) * cfg_scale */
+  float cfg_scale;
+  uint32_t flags;
+
+  /* ---- token history input_ids [B, ids_len] (CFG: one row per output row) ---- */
+  const void* input_ids;
+  int64_t ids_row_stride; /* elements */
+  int32_t ids_dtype;      /* MtrIdType */
+  int32_t ids_len;        /* L (0 allowed) */
+  int32_t penalty_start;  /* penalties use input_ids[:, penalty_start:] */
+
+  /* ---- monotonic time-shift mask ---- */
+  int32_t mono_mode; /* MtrMonoMode */
+  int32_t ts_start;  /* time-shift token ids are [ts_start, ts_end) */
+  int32_t ts_end;
+  int32_t n_sos;
+  int32_t sos_ids[MTR_MAX_SOS_IDS];
+  int32_t* mono_state; /* [B] */
+  float timeshift_bias; /* added to [ts_start, ts_end) when != 0 */
+
+  /* ---- event-grammar mask: allowed(v) = bit class_of[v] of allow[class_of[prev]] ---- */
+  const uint8_t* grammar_class_of; /* [V] or NULL (grammar off) */
+  const uint32_t* grammar_allow;   /* [grammar_n_classes] */
+  int32_t grammar_n_classes;
+  int32_t* prev_token; /* [B]; < 0 = no previous token (no mask) */
+
+  /* ---- penalties (off at 1 / 0 / 0) ---- */
+  float repetition_penalty;
+  float frequency_penalty;
+  float presence_penalty;
+
+  /* ---- temperature ---- */
+  int32_t temp_mode; /* MtrTempMode */
+  float temperature; /* base / scalar temperature (> 0) */
+  int32_t n_cond;
+  float cond_temperature[MTR_MAX_COND_TEMPS];
+  int32_t cond_offset[MTR_MAX_COND_TEMPS];              /* look at input_ids[row, L - offset] */
+  const uint32_t* cond_token_bits[MTR_MAX_COND_TEMPS];  /* [ceil(V/32)] membership bitmaps */
+  int32_t n_col_ranges;
+  int32_t col_start[MTR_MAX_COL_TEMP_RANGES];
+  int32_t col_end[MTR_MAX_COL_TEMP_RANGES];
+  float col_temperature[MTR_MAX_COL_TEMP_RANGES];
+
+  /* ---- selection ---- */
+  int32_t select_mode; /* MtrSelect */
+  int32_t top_k;       /* 0 = off */
+  float top_p;         /* 1 = off, else (0, 1) */
+  int32_t top_p_mode;  /* MtrTopPMode */
+  const float* uniforms; /* [B] in [0, 1); required for MTR_SELECT_SAMPLE */
+
+  /* ---- outputs ---- */
+  int64_t* out_ids; /* [B] */
+  float* out_scores; /* [B, V] processed scores (filtered = -inf) */
+  int64_t out_scores_row_stride;
+  float* out_logprobs; /* [B, V] log-softmax of the processed scores */
+  int64_t out_logprobs_row_stride;
+  uint32_t* out_status; /* [B] MTR_ROW_* bits */
+
+  /* ---- finished rows: token = unfinished ? drawn : pad_id; then unfinished &= !eos ---- */
+  uint8_t* unfinished; /* [B] or NULL */
+  int64_t pad_id;      /* also the token written for rows that cannot be sampled */
+  int32_t n_eos;
+  int32_t eos_ids[MTR_MAX_EOS_IDS];
+  int32_t n_eos_ranges;
+  int32_t eos_range_start[MTR_MAX_EOS_RANGES];
+  int32_t eos_range_end[MTR_MAX_EOS_RANGES];
+} MtrSamplerArgs;
+
+/* Launch geometry chosen for a problem size (diagnostics and tests). */
+typedef struct MtrLaunchInfo {
+  int32_t threads;        /* threads per CTA */
+  int32_t elems_per_thread;
+  int32_t cluster_size;   /* CTAs per row */
+  int32_t grid;           /* CTAs */
+  int32_t dyn_smem_bytes; /* dynamic shared memory per CTA */
+  int32_t max_vocab;      /* MTR_MAX_VOCAB */
+  int32_t max_ids_len;    /* MTR_MAX_IDS_LEN */
+  int32_t candidate_cap;  /* size of the exact in-bin candidate list */
+} MtrLaunchInfo;
+
+/* ABI identity: MTR_ABI_VERSION and sizeof(MtrSamplerArgs) of the library. */
+int mtr_abi_version(void);
+size_t mtr_args_size(void);
+
+/* Fill *args with defaults: everything off, temperature 1, top_p 1, pad 0. */
+int mtr_args_init(MtrSamplerArgs* args);
+
+/* Host-side argument checks only (no CUDA call). */
+int mtr_sampler_validate(const MtrSamplerArgs* args);
+
+/* Geometry the launcher would use for (vocab, num_rows, penalties on/off). */
+int mtr_sampler_query(int32_t vocab, int32_t num_rows, int32_t with_penalties, MtrLaunchInfo* out);
+
+/*
+ * Validate and enqueue the fused step on `stream` (a cudaStream_t; NULL = the
+ * legacy default stream).  The current CUDA device must own every pointer.
+ * Returns MTR_OK once the kernel is enqueued.  Capturable in a CUDA graph.
+ */
+int mtr_sampler_launch(const MtrSamplerArgs* args, void* stream);
+
+/* Human-readable name of an MtrStatus code. */
+const char* mtr_status_string(int code);
+
+/* Last cudaError_t seen by mtr_sampler_launch on this thread (0 = none). */
+int mtr_last_cuda_error(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MTR_SAMPLER_H */

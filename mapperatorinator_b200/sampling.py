@@ -1,0 +1,283 @@
+"""Sampler entry points: ``_sample`` and the stateful fused decode step.
+
+``_sample`` keeps the signature and semantics of the fast decode loop's
+sampler (osuT5/osuT5/inference/compiled_decode.py:1135-1158): greedy argmax,
+or temperature -> top-k -> top-p (descending-cumsum, shifted-by-one rule) ->
+draw, returning ``LongTensor[B, 1]``.  The draw is an inverse CDF in token-id
+order from caller-supplied uniforms (``uniforms=``), or from ``torch.rand``
+with ``generator=`` when none are given.
+
+:class:`FusedSampler` is the whole per-step tail of the decode loops
+(decode_loop.py:289-316, HF generation/utils.py:2762-2800) in one kernel:
+processor chain, draw, pad-on-finished, EOS tracking and the monotonic /
+grammar state updates, all on the device with no host synchronisation, so a
+step can be captured in a CUDA graph next to the decoder replay.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+
+from . import _native as N
+
+_TORCH_DTYPES = {torch.float32: N.DTYPE_F32, torch.bfloat16: N.DTYPE_BF16, torch.float16: N.DTYPE_F16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _TORCH_DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"logits dtype {t.dtype} is not supported (float32, bfloat16, float16)") from None
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{what} must be a CUDA tensor (the sampler has no CPU path)")
+
+
+def _ids_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.int64:
+        return N.IDS_I64
+    if t.dtype == torch.int32:
+        return N.IDS_I32
+    raise TypeError(f"input_ids dtype {t.dtype} is not supported (int64, int32)")
+
+
+def set_logits(args: N.MtrSamplerArgs, logits: torch.Tensor) -> None:
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("logits must be a 2-D tensor with unit stride along the vocabulary")
+    args.logits = logits.data_ptr()
+    args.logits_row_stride = logits.stride(0)
+    args.logits_dtype = dtype_code(logits)
+    args.vocab = logits.shape[1]
+
+
+def set_input_ids(args: N.MtrSamplerArgs, input_ids: torch.Tensor | None) -> None:
+    if input_ids is None:
+        args.input_ids = None
+        args.ids_len = 0
+        args.ids_row_stride = 0
+        return
+    if input_ids.dim() != 2 or (input_ids.shape[1] > 0 and input_ids.stride(1) != 1):
+        raise ValueError("input_ids must be [B, L] with unit stride along L")
+    _require_cuda(input_ids, "input_ids")
+    args.input_ids = input_ids.data_ptr() if input_ids.numel() else None
+    args.ids_dtype = _ids_code(input_ids)
+    args.ids_len = input_ids.shape[1]
+    args.ids_row_stride = input_ids.stride(0) if input_ids.shape[1] else 0
+
+
+def _uniforms(n: int, device, uniforms, generator) -> torch.Tensor:
+    if uniforms is None:
+        return torch.rand(n, device=device, generator=generator, dtype=torch.float32)
+    if uniforms.dtype != torch.float32 or uniforms.numel() != n:
+        raise ValueError(f"uniforms must be float32 with {n} elements")
+    _require_cuda(uniforms, "uniforms")
+    return uniforms.reshape(n).contiguous()
+
+
+def _sample(logits: torch.Tensor, do_sample: bool, top_p: float, top_k: int, temperature: float, *,
+            uniforms: torch.Tensor | None = None, generator: torch.Generator | None = None) -> torch.Tensor:
+    """Fused replacement of compiled_decode._sample; returns LongTensor[B, 1]."""
+    _require_cuda(logits, "logits")
+    B, V = logits.shape
+    args = N.new_args()
+    set_logits(args, logits)
+    args.num_rows = B
+    out = torch.empty(B, dtype=torch.int64, device=logits.device)
+    args.out_ids = out.data_ptr()
+    if not do_sample:
+        args.select_mode = N.SELECT_ARGMAX
+    else:
+        if not temperature > 0:
+            raise ValueError("temperature must be > 0")
+        args.select_mode = N.SELECT_SAMPLE
+        args.temperature = float(temperature)
+        if top_k > 0:
+            args.top_k = int(min(top_k, V))
+        if 0 < top_p < 1.0:
+            args.top_p = float(top_p)
+        args.top_p_mode = N.TOPP_SAMPLE_FN
+        u = _uniforms(B, logits.device, uniforms, generator)
+        args.uniforms = u.data_ptr()
+    N.launch(args, torch.cuda.current_stream(logits.device).cuda_stream)
+    return out.view(B, 1)
+
+
+def sample_next_tokens(scores: torch.Tensor, do_sample: bool, *, uniforms: torch.Tensor | None = None,
+                       generator: torch.Generator | None = None) -> torch.Tensor:
+    """softmax + multinomial (or argmax) of already-processed scores, as the
+    decode loops do after the processor list (decode_loop.py:296-301); [B]."""
+    return _sample(scores, do_sample, 1.0, 0, 1.0, uniforms=uniforms, generator=generator).view(-1)
+
+
+@dataclass
+class GrammarTable:
+    """Event-grammar mask: ``allow[c]`` has bit ``d`` set when a token of class
+    ``d`` may follow a token of class ``c``; ``class_of[v]`` is the class of id v."""
+
+    class_of: torch.Tensor  # [V] uint8
+    allow: torch.Tensor     # [C] int32 (bit patterns)
+
+    @classmethod
+    def from_bool_table(cls, class_of, table, device) -> "GrammarTable":
+        table = torch.as_tensor(table, dtype=torch.bool)
+        c = table.shape[0]
+        if table.shape != (c, c) or c > N.MAX_GRAMMAR_CLASSES:
+            raise ValueError("transition table must be square with at most 32 classes")
+        weights = (1 << torch.arange(c, dtype=torch.int64))
+        allow = (table.to(torch.int64) * weights).sum(1)
+        allow = torch.where(allow >= 2**31, allow - 2**32, allow).to(torch.int32)
+        return cls(torch.as_tensor(class_of, dtype=torch.uint8).to(device), allow.to(device))
+
+
+class FusedSampler:
+    """Stateful fused decode step for a fixed batch of ``num_rows`` rows.
+
+    Chain order: CFG -> monotonic time-shift mask -> timeshift bias -> grammar
+    mask -> repetition / frequency / presence penalties -> temperature ->
+    top-k -> top-p -> draw.  Device state per row: last time-shift value
+    (monotonic mask), previous token (grammar), unfinished flag.
+    """
+
+    def __init__(self, *, vocab_size: int, num_rows: int, device, cfg_scale: float = 1.0,
+                 time_shift_range: tuple[int, int] | None = None, sos_ids: Sequence[int] = (),
+                 timeshift_bias: float = 0.0, grammar: GrammarTable | None = None,
+                 repetition_penalty: float = 1.0, frequency_penalty: float = 0.0, presence_penalty: float = 0.0,
+                 penalty_start: int = 0, temperature: float = 1.0,
+                 conditional_temperatures: Sequence[tuple[float, int, torch.Tensor]] = (),
+                 column_temperatures: Sequence[tuple[int, int, float]] = (),
+                 top_k: int = 0, top_p: float = 1.0, top_p_mode: str = "hf", do_sample: bool = True,
+                 eos_token_ids: Sequence[int] = (), eos_ranges: Sequence[tuple[int, int]] = (),
+                 pad_token_id: int = 0, track_finished: bool = False,
+                 return_scores: bool = False, return_logprobs: bool = False):
+        self.device = torch.device(device)
+        self.vocab_size = int(vocab_size)
+        self.num_rows = int(num_rows)
+        B, V = self.num_rows, self.vocab_size
+        a = N.new_args()
+        a.num_rows = B
+        a.vocab = V
+        a.cfg_enabled = int(cfg_scale > 1.0)
+        a.cfg_scale = float(cfg_scale)
+        a.cfg_second_offset = B
+        self.mono_state = torch.full((B,), -1, dtype=torch.int32, device=self.device)
+        if time_shift_range is not None:
+            a.ts_start, a.ts_end = map(int, time_shift_range)
+            a.mono_mode = N.MONO_STATE
+            a.mono_state = self.mono_state.data_ptr()
+            if len(sos_ids) > N.MAX_SOS_IDS:
+                raise ValueError("at most 16 sos ids")
+            a.n_sos = len(sos_ids)
+            for i, t in enumerate(sos_ids):
+                a.sos_ids[i] = int(t)
+            a.flags |= N.FLAG_MONO_UPDATE_FROM_SAMPLE
+        a.timeshift_bias = float(timeshift_bias)
+        self.prev_token = torch.full((B,), -1, dtype=torch.int32, device=self.device)
+        self.grammar = grammar
+        if grammar is not None:
+            a.grammar_class_of = grammar.class_of.data_ptr()
+            a.grammar_allow = grammar.allow.data_ptr()
+            a.grammar_n_classes = grammar.allow.numel()
+            a.prev_token = self.prev_token.data_ptr()
+            a.flags |= N.FLAG_GRAMMAR_UPDATE_FROM_SAMPLE
+        a.repetition_penalty = float(repetition_penalty)
+        a.frequency_penalty = float(frequency_penalty)
+        a.presence_penalty = float(presence_penalty)
+        a.penalty_start = int(penalty_start)
+        a.temperature = float(temperature)
+        self._keep = []
+        if conditional_temperatures:
+            a.temp_mode = N.TEMP_ROW_CONDITIONAL
+            a.n_cond = len(conditional_temperatures)
+            for i, (t, off, bits) in enumerate(conditional_temperatures):
+                a.cond_temperature[i] = float(t)
+                a.cond_offset[i] = int(off)
+                bits = bits.to(self.device, torch.int32).contiguous()
+                self._keep.append(bits)
+                a.cond_token_bits[i] = bits.data_ptr()
+        elif column_temperatures:
+            a.temp_mode = N.TEMP_COLUMN_RANGES
+            a.n_col_ranges = len(column_temperatures)
+            for i, (s, e, t) in enumerate(column_temperatures):
+                a.col_start[i], a.col_end[i], a.col_temperature[i] = int(s), int(e), float(t)
+        a.select_mode = N.SELECT_SAMPLE if do_sample else N.SELECT_ARGMAX
+        a.top_k = int(top_k)
+        a.top_p = float(top_p)
+        a.top_p_mode = {"hf": N.TOPP_HF, "sample_fn": N.TOPP_SAMPLE_FN}[top_p_mode]
+        self.out_ids = torch.zeros(B, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(B, dtype=torch.int32, device=self.device)
+        a.out_ids = self.out_ids.data_ptr()
+        a.out_status = self.status.data_ptr()
+        self.scores = self.logprobs = None
+        if return_scores:
+            self.scores = torch.empty((B, V), dtype=torch.float32, device=self.device)
+            a.out_scores = self.scores.data_ptr()
+            a.out_scores_row_stride = V
+        if return_logprobs:
+            self.logprobs = torch.empty((B, V), dtype=torch.float32, device=self.device)
+            a.out_logprobs = self.logprobs.data_ptr()
+            a.out_logprobs_row_stride = V
+        self.unfinished = torch.ones(B, dtype=torch.uint8, device=self.device)
+        if track_finished:
+            a.unfinished = self.unfinished.data_ptr()
+        a.pad_id = int(pad_token_id)
+        if len(eos_token_ids) > N.MAX_EOS_IDS or len(eos_ranges) > N.MAX_EOS_RANGES:
+            raise ValueError("too many eos ids / ranges")
+        a.n_eos = len(eos_token_ids)
+        for i, t in enumerate(eos_token_ids):
+            a.eos_ids[i] = int(t)
+        a.n_eos_ranges = len(eos_ranges)
+        for i, (s, e) in enumerate(eos_ranges):
+            a.eos_range_start[i], a.eos_range_end[i] = int(s), int(e)
+        self._base = a
+        self._scan_next = time_shift_range is not None
+        self._prev_from_ids_next = grammar is not None
+
+    def reset(self) -> None:
+        """Forget per-row state; the next step re-derives it from input_ids."""
+        self.mono_state.fill_(-1)
+        self.prev_token.fill_(-1)
+        self.unfinished.fill_(1)
+        self._scan_next = self._base.mono_mode != N.MONO_OFF
+        self._prev_from_ids_next = self.grammar is not None
+
+    def _args(self, logits: torch.Tensor, input_ids, uniforms) -> N.MtrSamplerArgs:
+        a = N.MtrSamplerArgs()
+        ctypes.pointer(a)[0] = self._base
+        set_logits(a, logits)
+        if a.vocab != self.vocab_size:
+            raise ValueError(f"logits vocabulary {a.vocab} != {self.vocab_size}")
+        rows = logits.shape[0]
+        if rows != (2 * self.num_rows if a.cfg_enabled else self.num_rows):
+            raise ValueError(f"expected {2 * self.num_rows if a.cfg_enabled else self.num_rows} logits rows, got {rows}")
+        set_input_ids(a, input_ids)
+        if input_ids is not None and input_ids.shape[0] != self.num_rows:
+            raise ValueError("input_ids must have one row per output row")
+        if self._scan_next and input_ids is not None:
+            a.mono_mode = N.MONO_SCAN
+        if self._prev_from_ids_next and input_ids is not None and input_ids.shape[1] > 0:
+            a.flags |= N.FLAG_GRAMMAR_PREV_FROM_IDS
+        if a.select_mode == N.SELECT_SAMPLE:
+            a.uniforms = uniforms.data_ptr()
+        return a
+
+    def step(self, logits: torch.Tensor, input_ids: torch.Tensor | None = None,
+             uniforms: torch.Tensor | None = None, generator: torch.Generator | None = None) -> torch.Tensor:
+        """Process one decoder step's logits ([B, V], or [2B, V] with CFG) and
+        return the next tokens ``LongTensor[B]`` (a view of an internal buffer
+        that the next step overwrites)."""
+        _require_cuda(logits, "logits")
+        if self._base.select_mode == N.SELECT_SAMPLE:
+            uniforms = _uniforms(self.num_rows, logits.device, uniforms, generator)
+        a = self._args(logits, input_ids, uniforms)
+        N.launch(a, torch.cuda.current_stream(logits.device).cuda_stream)
+        if input_ids is not None:
+            self._scan_next = False
+            self._prev_from_ids_next = False
+        self._last_uniforms = uniforms  # keep alive until the kernel has consumed them
+        return self.out_ids

@@ -1,0 +1,99 @@
+"""Load the reference fixtures and turn each chain case into StepInputs."""
+
+from __future__ import annotations
+
+import json
+from functools import lru_cache
+from pathlib import Path
+
+import numpy as np
+
+from mapperatorinator_b200 import _native as N
+from mapperatorinator_b200.workloads import StepInputs, bf16_bits
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "reference_chain.npz"
+CHAIN_CASES = ("chain_cfg_mono_temp", "chain_condtemp", "chain_condtemp_b1", "chain_bias_cfg2", "chain_c0_shape",
+               "chain_c1_bf16")
+
+
+@lru_cache(maxsize=1)
+def fixtures():
+    z = np.load(GOLDEN)
+    data = {k: z[k] for k in z.files}
+    meta = json.loads(bytes(data.pop("meta.json")).decode())
+    return data, meta
+
+
+def case(name: str) -> dict:
+    data, meta = fixtures()
+    out = {k.split(".", 1)[1]: v for k, v in data.items() if k.startswith(name + ".")}
+    out["meta"] = meta.get(name, {})
+    return out
+
+
+def bits_for(ids, vocab):
+    words = np.zeros((vocab + 31) // 32, dtype=np.uint32)
+    for t in ids:
+        words[t >> 5] |= np.uint32(1 << (t & 31))
+    return words
+
+
+def conditionals(meta: dict, vocab: int):
+    """The reference's conditional temperature list (logit_processors.py:61-66)."""
+    t, tt, mt, kt = meta["temps"]
+    tt = t if tt is None else tt
+    mt = t if mt is None else mt
+    kt = t if kt is None else kt
+    ex = meta.get("extra", {})
+    conds = []
+    beat = [ex[k][0] for k in ("BEAT", "MEASURE") if k in ex]
+    if "TIMING_POINT" in ex:
+        beat.append(ex["TIMING_POINT"][0])
+    mania = [ex[k][0] for k in ("CIRCLE", "HOLD_NOTE", "HOLD_NOTE_END")] if "HOLD_NOTE_END" in ex else []
+    taiko = list(range(*ex["SCROLL_SPEED"])) if "SCROLL_SPEED" in ex else []
+    if tt != t and beat:
+        conds.append((tt, 1, bits_for(beat, vocab)))
+    if mt != t and mania:
+        conds.append((mt, 3, bits_for(mania, vocab)))
+    if kt != t and taiko:
+        conds.append((kt, 1, bits_for(taiko, vocab)))
+    return conds
+
+
+def chain_step(name: str, *, select_mode=N.SELECT_NONE, top_k=0, top_p=1.0, top_p_mode=N.TOPP_HF) -> StepInputs:
+    c = case(name)
+    m = c["meta"]
+    V, B = m["V"], m["B"]
+    x = c["logits"].astype(np.float32)
+    dtype = m.get("dtype", "f32")
+    logits = bf16_bits(x) if dtype == "bf16" else x
+    temps = m["temps"]
+    if m["types_first"]:
+        temp_mode, conds = N.TEMP_ROW_CONDITIONAL, conditionals(m, V)
+    else:
+        temp_mode, conds = N.TEMP_SCALAR, []
+    return StepInputs(
+        logits=logits, dtype=dtype, num_rows=B, cfg_scale=m["cfg"], input_ids=c["input_ids"].astype(np.int64),
+        mono_mode=N.MONO_SCAN, ts_start=m["ts"][0], ts_end=m["ts"][1], sos_ids=tuple(m["sos"]),
+        timeshift_bias=m["bias"], temp_mode=temp_mode, temperature=temps[0], cond=conds,
+        select_mode=select_mode, top_k=top_k, top_p=top_p, top_p_mode=top_p_mode,
+        uniforms=np.zeros(B, dtype=np.float32), want_scores=True,
+    )
+
+
+def explain_keep_mismatch(scores: np.ndarray, ref_keep: np.ndarray, got_keep: np.ndarray, top_p: float,
+                          status: int, margin: float = 1e-5) -> bool:
+    """True when a keep-set difference in one row is a tie at the cut or a
+    cumulative mass within `margin` of top_p (float64 reference mass)."""
+    if status & N.ROW_TIE_AT_CUT:
+        return True
+    fin = np.isfinite(scores)
+    x = scores[fin].astype(np.float64)
+    ids = np.nonzero(fin)[0]
+    p = np.exp(x - x.max())
+    p /= p.sum()
+    order = np.lexsort((ids, -x))
+    above = np.concatenate([[0.0], np.cumsum(p[order])[:-1]])
+    diff = np.nonzero(ref_keep != got_keep)[0]
+    pos = {int(t): i for i, t in enumerate(ids[order])}
+    return all(abs(above[pos[int(t)]] - top_p) < margin for t in diff if int(t) in pos)

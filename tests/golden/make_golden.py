@@ -1,0 +1,246 @@
+"""Generate the golden fixtures that pin the CPU oracle to the reference.
+
+Run in a checkout that has the Mapperatorinator sources (default
+/root/reference, override with MTR_REFERENCE_DIR) and the transformers
+package installed:
+
+    python tests/golden/make_golden.py
+
+It imports the reference's own processor modules by path -- the package
+``__init__`` files pull in dependencies that are not needed here, so the
+package roots are stubbed, as the reference's own tests do
+(tests/test_logit_processors.py:11-29) -- together with the installed HF
+warpers, runs them on seeded inputs and writes ``reference_chain.npz`` next
+to this script.  ``_sample`` (osuT5/osuT5/inference/compiled_decode.py:1135)
+is executed from the reference source with ``torch.multinomial`` observed, so
+its keep set is recorded without changing its code.
+
+The fixtures hold inputs and reference outputs only; the test suite never
+reads the reference checkout.
+"""
+
+from __future__ import annotations
+
+import ast
+import json
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REF = Path(os.environ.get("MTR_REFERENCE_DIR", "/root/reference"))
+OUT = Path(__file__).resolve().parent / "reference_chain.npz"
+
+
+def _stub_pkg(name: str, path: Path) -> None:
+    mod = types.ModuleType(name)
+    mod.__path__ = [str(path)]
+    sys.modules[name] = mod
+
+
+def load_reference():
+    _stub_pkg("osuT5", REF / "osuT5")
+    _stub_pkg("osuT5.osuT5", REF / "osuT5" / "osuT5")
+    _stub_pkg("osuT5.osuT5.inference", REF / "osuT5" / "osuT5" / "inference")
+    _stub_pkg("osuT5.osuT5.inference.optimized", REF / "osuT5" / "osuT5" / "inference" / "optimized")
+    _stub_pkg("osuT5.osuT5.inference.optimized.single",
+              REF / "osuT5" / "osuT5" / "inference" / "optimized" / "single")
+    _stub_pkg("osuT5.osuT5.dataset", REF / "osuT5" / "osuT5" / "dataset")
+    du = types.ModuleType("osuT5.osuT5.dataset.data_utils")
+    du.TIMED_EVENTS = []
+    sys.modules[du.__name__] = du
+    tk = types.ModuleType("osuT5.osuT5.tokenizer")
+    tk.MILISECONDS_PER_STEP = 10
+    tk.Tokenizer = object
+    sys.modules[tk.__name__] = tk
+    import osuT5.osuT5.event as ev
+    import osuT5.osuT5.inference.logit_processors as lp
+    import osuT5.osuT5.inference.optimized.single.logits as sl
+
+    src = (REF / "osuT5" / "osuT5" / "inference" / "compiled_decode.py").read_text()
+    tree = ast.parse(src)
+    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "_sample")
+    return ev, lp, sl, ast.Module(body=[fn], type_ignores=[])
+
+
+class _TorchObserver:
+    """Forwards to torch; records the probabilities handed to multinomial."""
+
+    def __init__(self):
+        self.probs = None
+
+    def __getattr__(self, name):
+        return getattr(torch, name)
+
+    def multinomial(self, probs, num_samples):
+        self.probs = probs.clone()
+        return torch.multinomial(probs, num_samples)
+
+
+def run_sample(fn_module, logits, do_sample, top_p, top_k, temperature):
+    obs = _TorchObserver()
+    ns = {"torch": obs, "F": torch.nn.functional}
+    exec(compile(fn_module, "compiled_decode._sample", "exec"), ns)
+    out = ns["_sample"](logits.clone(), do_sample, top_p, top_k, temperature)
+    return out, obs.probs
+
+
+def make_tokenizer(ev, *, ts=(16, 116), sos=1, context_sos=None, extra=None):
+    class Tok:
+        pass
+
+    t = Tok()
+    t.sos_id = sos
+    t.eos_id = 2
+    t.context_sos = dict(context_sos or {})
+    t.context_eos = {}
+    t.event_start = {ev.EventType.TIME_SHIFT: ts[0]}
+    t.event_end = {ev.EventType.TIME_SHIFT: ts[1]}
+    for name, (a, b) in (extra or {}).items():
+        t.event_start[ev.EventType[name]] = a
+        t.event_end[ev.EventType[name]] = b
+    return t
+
+
+def hf_warpers(scores, top_k, top_p):
+    from transformers import TopKLogitsWarper, TopPLogitsWarper
+
+    if top_k:
+        scores = TopKLogitsWarper(top_k=top_k, min_tokens_to_keep=1)(None, scores)
+    if top_p < 1.0:
+        scores = TopPLogitsWarper(top_p=top_p, min_tokens_to_keep=1)(None, scores)
+    return scores
+
+
+def main() -> None:
+    ev, lp, sl, sample_mod = load_reference()
+    g = torch.Generator().manual_seed(20240611)
+    fixtures: dict[str, np.ndarray] = {}
+    meta: dict[str, dict] = {}
+
+    def put(name, **arrays):
+        for k, v in arrays.items():
+            fixtures[f"{name}.{k}"] = np.asarray(v)
+
+    # ---- the reference's own test vectors (tests/test_logit_processors.py) ----
+    tok64 = make_tokenizer(ev, ts=(10, 20), sos=1)
+    mono = lp.MonotonicTimeShiftLogitsProcessor(tok64)
+    ids = torch.tensor([[1, 12, 5, 15, 3]])
+    sc = torch.arange(64, dtype=torch.float32).reshape(1, 64) / 10
+    put("ref_mono_vector", input_ids=ids.numpy(), scores=sc.numpy(), out=mono(ids.clone(), sc.clone()).numpy())
+    meta["ref_mono_vector"] = {"ts": [10, 20], "sos": [1]}
+
+    ct = lp.ConditionalTemperatureLogitsWarper(1.0, 2.0, 4.0, 8.0, True, (10, 11), (20,), (30,))
+    ids = torch.tensor([[0, 0, 10], [20, 0, 0], [0, 0, 30], [20, 0, 10], [0, 0, 0]])
+    sc = torch.full((5, 4), 8.0)
+    put("ref_condtemp_batch", input_ids=ids.numpy(), scores=sc.numpy(), out=ct(ids, sc).numpy())
+    meta["ref_condtemp_batch"] = {"temps": [1.0, 2.0, 4.0, 8.0], "beat": [10, 11], "mania": [20], "taiko": [30]}
+
+    # stateful monotonic over growing prefixes and random trials
+    seq = torch.tensor([[1, 12, 5, 11, 7, 15, 3, 1, 14, 9]])
+    st = sl.MonotonicTimeShiftLogitsProcessor(tok64)
+    outs = []
+    for n in range(1, seq.shape[1] + 1):
+        s0 = torch.arange(64, dtype=torch.float32).reshape(1, 64) / 10
+        outs.append(st(seq[:, :n].clone(), s0.clone()).numpy()[0])
+    put("ref_stateful_prefixes", input_ids=seq.numpy(), out=np.stack(outs))
+    for bsz in (1, 2, 5):
+        gen = torch.Generator().manual_seed(34567 + bsz)
+        trial_ids, trial_scores, trial_out, lens = [], [], [], []
+        for _ in range(32):
+            L = int(torch.randint(1, 48, (), generator=gen).item())
+            ii = torch.randint(0, 30, (bsz, L), generator=gen)
+            ss = torch.randn((bsz, 64), generator=gen)
+            trial_ids.append(np.pad(ii.numpy(), ((0, 0), (0, 48 - L)), constant_values=-1))
+            trial_scores.append(ss.numpy())
+            trial_out.append(mono(ii.clone(), ss.clone()).numpy())
+            lens.append(L)
+        put(f"ref_random_b{bsz}", input_ids=np.stack(trial_ids), scores=np.stack(trial_scores),
+            out=np.stack(trial_out), lens=np.array(lens))
+
+    # ---- full chains: build_logits_processor_list + HF warpers / _sample ----
+    def chain_case(name, *, B, V, L, cfg, ts, sos, ctx_sos, types_first, temps, bias, top_k, top_p,
+                   dtype="f32", extra=None, spikes=0, sigma=1.5, history_fn=None):
+        tok = make_tokenizer(ev, ts=ts, sos=sos, context_sos=ctx_sos, extra=extra)
+        R = 2 * B if cfg > 1.0 else B
+        x = torch.randn((R, V), generator=g) * sigma
+        if spikes:
+            sid = torch.randperm(V, generator=g)[:spikes]
+            x[:, sid] = 8.0
+        if dtype == "bf16":
+            x = x.to(torch.bfloat16).to(torch.float32)
+        ids = history_fn(B, L) if history_fn else torch.randint(0, V, (B, L), generator=g)
+        procs = lp.build_logits_processor_list(
+            tok, cfg_scale=cfg, timeshift_bias=bias, types_first=types_first, temperature=temps[0],
+            timing_temperature=temps[1], mania_column_temperature=temps[2], taiko_hit_temperature=temps[3])
+        processed = procs(ids.clone(), x.clone())
+        final = hf_warpers(processed.clone(), top_k, top_p)
+        _, probs = run_sample(sample_mod, processed.clone(), True, top_p, top_k, 1.0)
+        greedy, _ = run_sample(sample_mod, processed.clone(), False, top_p, top_k, 1.0)
+        put(name, logits=x.numpy(), input_ids=ids.numpy(), processed=processed.numpy(), final_hf=final.numpy(),
+            sample_fn_probs=probs.numpy(), greedy=greedy.numpy())
+        meta[name] = {"B": B, "V": V, "cfg": cfg, "ts": list(ts), "sos": [sos] + list((ctx_sos or {}).values()),
+                      "types_first": types_first, "temps": list(temps), "bias": bias, "top_k": top_k,
+                      "top_p": top_p, "dtype": dtype,
+                      "extra": {k: list(v) for k, v in (extra or {}).items()}}
+
+    def ts_heavy_history(B, L, V=256, ts=(16, 116), sos=(1, 3)):
+        h = torch.randint(120, V, (B, L), generator=g)
+        for b in range(B):
+            k = int(torch.randint(0, 4, (), generator=g))
+            pos = torch.randperm(L, generator=g)[:6]
+            h[b, pos] = torch.randint(ts[0], ts[1], (6,), generator=g)
+            if k == 0:
+                h[b, -1] = sos[0]
+            if k == 1:
+                h[b, int(pos.max()) - 1 if int(pos.max()) > 0 else 0] = sos[1]
+        return h
+
+    ctx = {ev.ContextType.TIMING: 3}
+    chain_case("chain_cfg_mono_temp", B=4, V=256, L=24, cfg=1.5, ts=(16, 116), sos=1, ctx_sos=ctx, types_first=False,
+               temps=(0.9, None, None, None), bias=0.0, top_k=0, top_p=0.9, history_fn=ts_heavy_history)
+    extra = {"BEAT": (130, 131), "MEASURE": (131, 132), "TIMING_POINT": (132, 133), "CIRCLE": (140, 141),
+             "HOLD_NOTE": (141, 142), "HOLD_NOTE_END": (142, 143), "SCROLL_SPEED": (150, 170)}
+
+    def cond_history(B, L):
+        h = torch.randint(0, 256, (B, L), generator=g)
+        picks = [130, 131, 132, 140, 141, 142, 155, 169, 7, 200]
+        for b in range(B):
+            h[b, -1] = picks[b % len(picks)]
+            h[b, -3] = picks[(3 * b + 1) % len(picks)]
+        return h
+
+    chain_case("chain_condtemp", B=10, V=256, L=12, cfg=1.0, ts=(16, 116), sos=1, ctx_sos=None, types_first=True,
+               temps=(1.0, 0.7, 1.3, 1.1), bias=0.0, top_k=10, top_p=0.8, extra=extra, history_fn=cond_history)
+    chain_case("chain_condtemp_b1", B=1, V=256, L=12, cfg=1.0, ts=(16, 116), sos=1, ctx_sos=None, types_first=True,
+               temps=(1.0, 0.7, 1.3, 1.1), bias=0.0, top_k=0, top_p=0.95, extra=extra,
+               history_fn=lambda B, L: torch.tensor([[5] * (L - 1) + [131]]))
+    chain_case("chain_bias_cfg2", B=3, V=256, L=16, cfg=2.0, ts=(16, 116), sos=1, ctx_sos=None, types_first=False,
+               temps=(1.2, None, None, None), bias=0.5, top_k=5, top_p=1.0, history_fn=ts_heavy_history)
+    chain_case("chain_c0_shape", B=1, V=4096, L=32, cfg=1.5, ts=(0, 2000), sos=4094, ctx_sos=None,
+               types_first=False, temps=(0.9, None, None, None), bias=0.0, top_k=0, top_p=0.9, spikes=8)
+    chain_case("chain_c1_bf16", B=2, V=4096, L=32, cfg=1.5, ts=(0, 2000), sos=4094, ctx_sos=None,
+               types_first=False, temps=(0.9, None, None, None), bias=0.0, top_k=0, top_p=0.9, spikes=8,
+               dtype="bf16")
+
+    # ---- HF repetition penalty + top-k + top-p (third-party processors the chain appends) ----
+    from transformers import RepetitionPenaltyLogitsProcessor
+
+    B, V, L = 4, 512, 64
+    x = (torch.randn((B, V), generator=g) * 2.0).to(torch.bfloat16).to(torch.float32)
+    ids = torch.randint(0, V, (B, L), generator=g)
+    rep = RepetitionPenaltyLogitsProcessor(1.1)(ids, x.clone())
+    put("hf_repetition", logits=x.numpy(), input_ids=ids.numpy(), processed=rep.numpy(),
+        final_hf=hf_warpers(rep.clone(), 50, 0.95).numpy())
+    meta["hf_repetition"] = {"penalty": 1.1, "top_k": 50, "top_p": 0.95}
+
+    fixtures["meta.json"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+    np.savez_compressed(OUT, **fixtures)
+    print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(fixtures)} arrays)")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,148 @@
+"""The C-ABI library loads on a CPU-only host, exports every symbol the header
+declares and rejects invalid arguments before any CUDA call."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from mapperatorinator_b200 import _native as N
+from mapperatorinator_b200 import build as B
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "mtr_sampler.h"
+
+
+def header_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(mtr_\w+)\s*\(", text, flags=re.M)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    B.build()
+    return N.load()
+
+
+def test_header_symbols_exported(lib):
+    names = header_functions()
+    assert names, "no declarations parsed"
+    assert set(names) == set(N.EXPORTS), (names, sorted(N.EXPORTS))
+    for n in names:
+        assert hasattr(lib, n), n
+
+
+def test_struct_layout(lib):
+    assert lib.mtr_abi_version() == N.ABI_VERSION
+    assert lib.mtr_args_size() == ctypes.sizeof(N.MtrSamplerArgs)
+
+
+def test_args_init_defaults(lib):
+    a = N.new_args()
+    assert a.abi_version == N.ABI_VERSION and a.struct_size == ctypes.sizeof(a)
+    assert a.temperature == 1.0 and a.top_p == 1.0 and a.repetition_penalty == 1.0
+    assert a.select_mode == N.SELECT_NONE and a.mono_mode == N.MONO_OFF
+
+
+def _valid_args():
+    a = N.new_args()
+    a.logits = 0x10000
+    a.logits_row_stride = 4096
+    a.logits_dtype = N.DTYPE_BF16
+    a.num_rows = 4
+    a.vocab = 4096
+    a.select_mode = N.SELECT_SAMPLE
+    a.uniforms = 0x20000
+    a.out_ids = 0x30000
+    return a
+
+
+def test_validate_accepts_valid(lib):
+    assert N.validate(_valid_args()) == N.OK
+
+
+@pytest.mark.parametrize(
+    "field,value,code",
+    [
+        ("vocab", 0, N.ERR_BAD_SHAPE),
+        ("vocab", N.MAX_VOCAB + 1, N.ERR_BAD_SHAPE),
+        ("num_rows", -1, N.ERR_BAD_SHAPE),
+        ("logits", 0, N.ERR_NULL_ARG),
+        ("logits", 0x10001, N.ERR_ALIGNMENT),
+        ("logits_row_stride", 100, N.ERR_BAD_SHAPE),
+        ("logits_dtype", 9, N.ERR_BAD_PARAM),
+        ("top_p", 0.0, N.ERR_BAD_PARAM),
+        ("top_p", 1.5, N.ERR_BAD_PARAM),
+        ("top_k", -1, N.ERR_BAD_PARAM),
+        ("temperature", 0.0, N.ERR_BAD_PARAM),
+        ("temperature", float("nan"), N.ERR_BAD_PARAM),
+        ("repetition_penalty", 0.0, N.ERR_BAD_PARAM),
+        ("frequency_penalty", float("inf"), N.ERR_BAD_PARAM),
+        ("uniforms", 0, N.ERR_NULL_ARG),
+        ("out_ids", 0, N.ERR_NULL_ARG),
+        ("select_mode", 7, N.ERR_BAD_PARAM),
+        ("top_p_mode", 5, N.ERR_BAD_PARAM),
+        ("mono_mode", N.MONO_STATE, N.ERR_NULL_ARG),
+        ("ts_end", 5000, N.ERR_BAD_SHAPE),
+        ("flags", 1 << 20, N.ERR_BAD_PARAM),
+        ("abi_version", 99, N.ERR_ABI),
+        ("ids_len", N.MAX_IDS_LEN + 1, N.ERR_BAD_SHAPE),
+        ("n_sos", 17, N.ERR_BAD_PARAM),
+        ("n_eos", 17, N.ERR_BAD_PARAM),
+        ("cfg_scale", float("nan"), N.ERR_BAD_PARAM),
+    ],
+)
+def test_validate_rejects(lib, field, value, code):
+    a = _valid_args()
+    if field == "cfg_scale":
+        a.cfg_enabled = 1
+    setattr(a, field, value)
+    assert N.validate(a) == code
+    # the launcher validates first, so no CUDA call is made for bad input
+    assert lib.mtr_sampler_launch(ctypes.byref(a), None) == code
+
+
+def test_penalties_need_history(lib):
+    a = _valid_args()
+    a.repetition_penalty = 1.1
+    a.ids_len = 16
+    assert N.validate(a) == N.ERR_NULL_ARG
+
+
+def test_grammar_requirements(lib):
+    a = _valid_args()
+    a.grammar_class_of = 0x40000
+    assert N.validate(a) == N.ERR_NULL_ARG
+    a.grammar_allow = 0x50000
+    a.grammar_n_classes = 40
+    assert N.validate(a) == N.ERR_BAD_PARAM
+    a.grammar_n_classes = 16
+    assert N.validate(a) == N.ERR_NULL_ARG  # prev_token missing
+    a.flags = N.FLAG_GRAMMAR_PREV_FROM_IDS
+    assert N.validate(a) == N.OK
+
+
+def test_zero_rows_is_a_noop(lib):
+    a = _valid_args()
+    a.num_rows = 0
+    assert lib.mtr_sampler_launch(ctypes.byref(a), None) == N.OK
+
+
+@pytest.mark.parametrize("vocab,cs", [(1, 1), (4096, 1), (4097, 2), (8192, 2), (16384, 4), (65536, 8),
+                                      (131072, 8)])
+def test_query_geometry(lib, vocab, cs):
+    info = N.query(vocab, 10, True)
+    assert info.cluster_size == cs
+    assert info.threads * info.elems_per_thread * info.cluster_size >= vocab
+    assert info.grid == 10 * cs
+    assert info.candidate_cap == 256
+    assert info.dyn_smem_bytes == info.threads * info.elems_per_thread * 10
+
+
+def test_status_strings(lib):
+    assert N.status_string(N.OK) == "MTR_OK"
+    assert N.status_string(N.ERR_ABI) == "MTR_ERR_ABI"
+    with pytest.raises(ValueError):
+        N.check(N.ERR_BAD_PARAM)

@@ -1,0 +1,266 @@
+"""Kernel vs CPU oracle through the C ABI (bit-exact ids, keep sets, states;
+log-probs within 1e-5 relative + 1e-6 absolute)."""
+
+import numpy as np
+import pytest
+
+from mapperatorinator_b200 import _native as N
+from mapperatorinator_b200 import workloads as W
+from mapperatorinator_b200.stepargs import DeviceStep
+from oracle import oracle
+from tests import _golden as G
+
+pytestmark = pytest.mark.gpu
+
+
+def run_both(s, device):
+    import torch
+
+    ref = oracle.run(s)
+    dev = DeviceStep(s, device)
+    dev.launch()
+    torch.cuda.synchronize(device)
+    return ref, dev.results()
+
+
+def assert_parity(s, device):
+    ref, got = run_both(s, device)
+    errs = oracle.compare(ref, got)
+    assert not errs, "\n".join(errs)
+    return ref, got
+
+
+# ---------------------------------------------------------------- workloads
+@pytest.mark.parametrize("want", [(False, False), (True, True)])
+def test_cfg_pair_fp32(cuda_device, want):
+    for seed in range(8):
+        s = W.cfg_pair_fp32(seed).with_(want_scores=want[0], want_logprobs=want[1])
+        assert_parity(s, cuda_device)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_batched_decode(cuda_device, dtype):
+    s = W.batched_decode(seed=11, pairs=64, dtype=dtype).with_(want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+
+
+def test_penalty_sweep(cuda_device):
+    s = W.penalty_sweep(seed=12, rows=512).with_(want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+
+
+def test_sharded_decode_full_size(cuda_device):
+    s = W.sharded_decode(seed=13, pairs=4096)
+    ref, got = assert_parity(s, cuda_device)
+    assert (got["out_status"] & (N.ROW_NONFINITE | N.ROW_ALL_MASKED) == 0).all()
+
+
+@pytest.mark.parametrize("vocab", [8192, 16384, 32768, 65536, 131072])
+def test_vocab_sweep_clusters(cuda_device, vocab):
+    rows = 64 if vocab <= 65536 else 16
+    s = W.penalty_sweep(seed=vocab, rows=rows, vocab=vocab, history=256).with_(want_scores=True)
+    assert_parity(s, cuda_device)
+    s2 = W.batched_decode(seed=vocab + 1, pairs=rows // 2, vocab=vocab).with_(want_scores=True, want_logprobs=True)
+    assert_parity(s2, cuda_device)
+
+
+# ---------------------------------------------------------------- modes
+@pytest.mark.parametrize("mode", [N.SELECT_NONE, N.SELECT_ARGMAX, N.SELECT_SAMPLE])
+@pytest.mark.parametrize("topp_mode", [N.TOPP_HF, N.TOPP_SAMPLE_FN])
+def test_select_modes(cuda_device, mode, topp_mode):
+    s = W.batched_decode(seed=21, pairs=96).with_(select_mode=mode, top_p_mode=topp_mode, top_k=40,
+                                                   want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+
+
+@pytest.mark.parametrize("top_k,top_p", [(1, 1.0), (5, 1.0), (0, 0.5), (0, 1e-4), (0, 0.999999), (4095, 0.9),
+                                         (4096, 0.9), (10000, 0.9), (300, 0.97), (0, 1.0)])
+def test_topk_topp_grid(cuda_device, top_k, top_p):
+    s = W.penalty_sweep(seed=31, rows=128).with_(top_k=top_k, top_p=top_p, want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+
+
+def test_force_radix_paths(cuda_device):
+    for s in (W.penalty_sweep(seed=41, rows=128), W.batched_decode(seed=42, pairs=64),
+              W.penalty_sweep(seed=43, rows=64, vocab=16384, history=128)):
+        s = s.with_(flags=s.flags | N.FLAG_FORCE_RADIX, want_scores=True, want_logprobs=True)
+        ref, got = assert_parity(s, cuda_device)
+        assert (got["out_status"] & N.ROW_SLOW_PATH).any()
+
+
+def test_wide_nucleus_dense_path(cuda_device):
+    # fp32, low temperature spread: thousands of survivors -> dense top-p and draw
+    rng = np.random.default_rng(5)
+    x = rng.normal(0, 0.3, size=(200, 4096)).astype(np.float32)
+    s = W.StepInputs(logits=x, dtype="f32", num_rows=200, select_mode=N.SELECT_SAMPLE, top_p=0.99,
+                     uniforms=rng.random(200, dtype=np.float32), want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+    assert_parity(s.with_(top_p=1.0), cuda_device)
+
+
+# ---------------------------------------------------------------- edge cases
+@pytest.mark.parametrize("vocab", [1, 2, 7, 33, 1000, 4099, 5000])
+@pytest.mark.parametrize("dtype", ["f32", "bf16", "f16"])
+def test_ragged_vocab_and_dtypes(cuda_device, vocab, dtype):
+    rng = np.random.default_rng(vocab)
+    rows = 9
+    x = rng.normal(0, 2, size=(2 * rows, vocab)).astype(np.float32)
+    logits = {"f32": x, "bf16": W.bf16_bits(x), "f16": x.astype(np.float16)}[dtype]
+    ids = rng.integers(0, vocab, size=(rows, 17)).astype(np.int64)
+    s = W.StepInputs(logits=logits, dtype=dtype, num_rows=rows, cfg_scale=1.3, input_ids=ids,
+                     repetition_penalty=1.2, frequency_penalty=0.1, presence_penalty=0.05,
+                     mono_mode=N.MONO_SCAN, ts_start=0, ts_end=max(1, vocab // 2), sos_ids=(vocab - 1,),
+                     temperature=0.8, select_mode=N.SELECT_SAMPLE, top_k=min(5, vocab), top_p=0.9,
+                     uniforms=rng.random(rows, dtype=np.float32), want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+
+
+def test_masked_nan_inf_rows(cuda_device):
+    rng = np.random.default_rng(7)
+    x = rng.normal(0, 1, size=(6, 256)).astype(np.float32)
+    x[0, :] = -np.inf            # all masked
+    x[1, 17] = np.nan            # NaN
+    x[2, 3] = np.inf             # +inf
+    x[3, :] = -np.inf
+    x[3, 200] = 0.5              # single survivor
+    x[4, 10:20] = np.nan
+    for mode in (N.SELECT_SAMPLE, N.SELECT_ARGMAX, N.SELECT_NONE):
+        s = W.StepInputs(logits=x, dtype="f32", num_rows=6, select_mode=mode, top_p=0.9, pad_id=3,
+                         uniforms=rng.random(6, dtype=np.float32), want_scores=True, want_logprobs=True)
+        ref, got = assert_parity(s, cuda_device)
+        if mode == N.SELECT_ARGMAX:
+            assert got["out_ids"][0] == 0 and got["out_ids"][1] == 17 and got["out_ids"][2] == 3
+        assert got["out_status"][0] & N.ROW_ALL_MASKED
+        assert got["out_status"][1] & N.ROW_NONFINITE
+
+
+def test_ties_everywhere(cuda_device):
+    rng = np.random.default_rng(8)
+    x = rng.integers(-3, 4, size=(64, 4096)).astype(np.float32)
+    for tk, tp, mode in [(0, 0.5, N.TOPP_HF), (7, 1.0, N.TOPP_HF), (50, 0.3, N.TOPP_SAMPLE_FN), (0, 0.01, N.TOPP_HF)]:
+        s = W.StepInputs(logits=x, dtype="f32", num_rows=64, select_mode=N.SELECT_SAMPLE, top_k=tk, top_p=tp,
+                         top_p_mode=mode, uniforms=rng.random(64, dtype=np.float32), want_scores=True)
+        assert_parity(s, cuda_device)
+        assert_parity(s.with_(flags=N.FLAG_FORCE_RADIX), cuda_device)
+
+
+def test_uniform_extremes_and_bad_ids(cuda_device):
+    s = W.penalty_sweep(seed=51, rows=8)
+    ids = s.input_ids.copy()
+    ids[0, 5] = 4096
+    ids[1, 0] = -3
+    u = np.array([0.0, np.nextafter(np.float32(1), np.float32(0)), -0.5, 1.0, np.nan, 0.5, 0.25, 1e-30],
+                 dtype=np.float32)
+    ref, got = assert_parity(s.with_(input_ids=ids, uniforms=u), cuda_device)
+    assert got["out_status"][0] & N.ROW_BAD_ID and got["out_status"][1] & N.ROW_BAD_ID
+    assert got["out_status"][2] & N.ROW_BAD_UNIFORM and got["out_status"][4] & N.ROW_BAD_UNIFORM
+
+
+def test_empty_history_and_conditional_temperature(cuda_device):
+    rng = np.random.default_rng(9)
+    x = rng.normal(0, 2, size=(4, 512)).astype(np.float32)
+    conds = [(0.5, 1, G.bits_for([100, 101], 512)), (2.0, 3, G.bits_for([7], 512))]
+    for L in (0, 1, 2, 3, 9):
+        ids = rng.integers(0, 512, size=(4, L)).astype(np.int64)
+        if L >= 3:
+            ids[0, -1] = 100
+            ids[1, -3] = 7
+        s = W.StepInputs(logits=x, dtype="f32", num_rows=4, input_ids=ids, temp_mode=N.TEMP_ROW_CONDITIONAL,
+                         temperature=1.1, cond=conds, mono_mode=N.MONO_SCAN, ts_start=0, ts_end=256, sos_ids=(1,),
+                         flags=N.FLAG_GRAMMAR_PREV_FROM_IDS, grammar_class_of=(np.arange(512) % 4).astype(np.uint8),
+                         grammar_allow=np.array([0b0011, 0b0110, 0b1100, 0b1001], dtype=np.uint32),
+                         repetition_penalty=1.3, select_mode=N.SELECT_SAMPLE, top_p=0.8,
+                         uniforms=rng.random(4, dtype=np.float32), want_scores=True, want_logprobs=True)
+        assert_parity(s, cuda_device)
+
+
+def test_finished_rows_and_eos(cuda_device):
+    s = W.batched_decode(seed=61, pairs=32)
+    unf = np.ones(32, dtype=np.uint8)
+    unf[::3] = 0
+    s = s.with_(unfinished=unf, pad_id=7, eos_ids=(5, 9), eos_ranges=((0, 1000),),
+                flags=N.FLAG_MONO_UPDATE_FROM_SAMPLE | N.FLAG_GRAMMAR_UPDATE_FROM_SAMPLE)
+    ref, got = assert_parity(s, cuda_device)
+    assert (got["out_ids"][::3] == 7).all()
+
+
+# ---------------------------------------------------------------- multi-step state
+def test_state_carried_over_steps(cuda_device):
+    import torch
+
+    base = W.batched_decode(seed=71, pairs=48).with_(
+        flags=N.FLAG_MONO_UPDATE_FROM_SAMPLE | N.FLAG_GRAMMAR_UPDATE_FROM_SAMPLE, sos_ids=(4094, 3000))
+    rng = np.random.default_rng(72)
+    host = base
+    dev = None
+    for step in range(12):
+        x = rng.normal(0, 1.5, size=(96, 4096)).astype(np.float32)
+        u = rng.random(48, dtype=np.float32)
+        host = host.with_(logits=W.bf16_bits(x), uniforms=u)
+        ref = oracle.run(host)
+        dev = DeviceStep(host, cuda_device)
+        dev.launch()
+        torch.cuda.synchronize()
+        got = dev.results()
+        assert not oracle.compare(ref, got), step
+        host = host.with_(mono_state=ref["mono_state"], prev_token=ref["prev_token"])
+
+
+def test_scan_equals_incremental_state(cuda_device):
+    import torch
+
+    rng = np.random.default_rng(81)
+    B, V = 16, 256
+    ids = rng.integers(0, 40, size=(B, 30)).astype(np.int64)
+    x = rng.normal(0, 1, size=(B, V)).astype(np.float32)
+    state = None
+    for L in range(1, 31):
+        scan = W.StepInputs(logits=x, dtype="f32", num_rows=B, input_ids=np.ascontiguousarray(ids[:, :L]),
+                            mono_mode=N.MONO_SCAN, ts_start=10, ts_end=30, sos_ids=(1, 2),
+                            select_mode=N.SELECT_NONE, want_scores=True)
+        ref = oracle.run(scan)
+        if state is None:
+            inc = scan.with_(mono_state=np.full(B, -1, np.int32))
+        else:
+            inc = scan.with_(mono_mode=N.MONO_STATE, flags=N.FLAG_MONO_UPDATE_FROM_IDS, mono_state=state)
+        dev = DeviceStep(inc, cuda_device)
+        dev.launch()
+        torch.cuda.synchronize()
+        got = dev.results()
+        assert np.array_equal(got["out_scores"].view(np.uint32), ref["out_scores"].view(np.uint32)), L
+        state = got["mono_state"]
+
+
+# ---------------------------------------------------------------- reference fixtures on the GPU
+@pytest.mark.parametrize("name", G.CHAIN_CASES)
+def test_reference_fixture_processed_scores(cuda_device, name):
+    import torch
+
+    c = G.case(name)
+    dev = DeviceStep(G.chain_step(name), cuda_device)
+    dev.launch()
+    torch.cuda.synchronize()
+    got = dev.results()["out_scores"]
+    assert np.array_equal(got.view(np.uint32), c["processed"].view(np.uint32))
+    m = c["meta"]
+    s = G.chain_step(name, top_k=m["top_k"], top_p=m["top_p"])
+    assert_parity(s, cuda_device)
+
+
+# ---------------------------------------------------------------- graph capture
+def test_cuda_graph_capture_replay(cuda_device):
+    import torch
+
+    s = W.penalty_sweep(seed=91, rows=256)
+    dev = DeviceStep(s, cuda_device)
+    stream = torch.cuda.Stream(cuda_device)
+    dev.launch(stream)  # warm (sets kernel attributes outside capture)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        dev.launch(torch.cuda.current_stream())
+    dev.tensors["out_ids"].fill_(-1)
+    g.replay()
+    torch.cuda.synchronize()
+    ref = oracle.run(s)
+    assert np.array_equal(dev.results()["out_ids"], ref["out_ids"])

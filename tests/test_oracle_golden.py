@@ -1,0 +1,119 @@
+"""Pin the CPU oracle to the reference: fixtures produced by running the
+reference's own processors (tests/golden/make_golden.py).  CPU only."""
+
+import numpy as np
+import pytest
+
+from mapperatorinator_b200 import _native as N
+from oracle import oracle
+from tests import _golden as G
+
+
+def test_reference_monotonic_vector():
+    # tests/test_logit_processors.py:43-51: ids [1,12,5,15,3], TS 10..19 -> -inf on 10..14
+    c = G.case("ref_mono_vector")
+    s = G.StepInputs(logits=c["scores"], dtype="f32", num_rows=1, input_ids=c["input_ids"], mono_mode=N.MONO_SCAN,
+                     ts_start=10, ts_end=20, sos_ids=(1,), select_mode=N.SELECT_NONE, want_scores=True)
+    out = oracle.run(s)["out_scores"]
+    assert np.array_equal(out, c["out"])
+    assert np.isneginf(out[0, 10:15]).all()
+    assert np.array_equal(out[0, 15:], c["scores"][0, 15:])
+
+
+def test_reference_conditional_temperature_batch():
+    # tests/test_logit_processors.py:63-91: first-match precedence -> [4, 2, 1, 4, 8]
+    c = G.case("ref_condtemp_batch")
+    conds = [(2.0, 1, G.bits_for([10, 11], 64)), (4.0, 3, G.bits_for([20], 64)), (8.0, 1, G.bits_for([30], 64))]
+    logits = np.zeros((5, 64), dtype=np.float32)
+    logits[:, :4] = c["scores"]
+    s = G.StepInputs(logits=logits, dtype="f32", num_rows=5, input_ids=c["input_ids"], temp_mode=N.TEMP_ROW_CONDITIONAL,
+                     temperature=1.0, cond=conds, select_mode=N.SELECT_NONE, want_scores=True)
+    out = oracle.run(s)["out_scores"][:, :4]
+    assert np.array_equal(out, c["out"])
+    assert np.array_equal(out[:, 0], np.array([4.0, 2.0, 1.0, 4.0, 8.0], dtype=np.float32))
+
+
+def test_reference_stateful_prefixes_match_state_mode():
+    # optimized/single/logits.py stateful processor over growing prefixes
+    c = G.case("ref_stateful_prefixes")
+    seq = c["input_ids"]
+    scores = (np.arange(64, dtype=np.float32) / 10).reshape(1, 64)
+    state = np.array([-1], dtype=np.int32)
+    for n in range(1, seq.shape[1] + 1):
+        ids = seq[:, :n]
+        mode, flags = (N.MONO_SCAN, 0) if n == 1 else (N.MONO_STATE, N.FLAG_MONO_UPDATE_FROM_IDS)
+        s = G.StepInputs(logits=scores, dtype="f32", num_rows=1, input_ids=ids, mono_mode=mode, flags=flags,
+                         ts_start=10, ts_end=20, sos_ids=(1,), mono_state=state, select_mode=N.SELECT_NONE,
+                         want_scores=True)
+        r = oracle.run(s)
+        state = r["mono_state"]
+        assert np.array_equal(r["out_scores"][0], c["out"][n - 1]), n
+
+
+@pytest.mark.parametrize("bsz", [1, 2, 5])
+def test_reference_random_full_scan_trials(bsz):
+    # test_optimized_single_logits_migration.py:59-78 inputs, reference full-scan outputs
+    c = G.case(f"ref_random_b{bsz}")
+    for t in range(c["input_ids"].shape[0]):
+        L = int(c["lens"][t])
+        ids = np.ascontiguousarray(c["input_ids"][t, :, :L])
+        s = G.StepInputs(logits=c["scores"][t], dtype="f32", num_rows=bsz, input_ids=ids, mono_mode=N.MONO_SCAN,
+                         ts_start=10, ts_end=20, sos_ids=(1,), select_mode=N.SELECT_NONE, want_scores=True)
+        assert np.array_equal(oracle.run(s)["out_scores"], c["out"][t]), t
+
+
+@pytest.mark.parametrize("name", G.CHAIN_CASES)
+def test_chain_processed_scores_bit_exact(name):
+    # CFG -> monotonic -> [bias] -> temperature, exactly as build_logits_processor_list
+    c = G.case(name)
+    out = oracle.run(G.chain_step(name))["out_scores"]
+    ref = c["processed"]
+    assert out.view(np.uint32).tolist() == ref.view(np.uint32).tolist() or np.array_equal(out, ref)
+
+
+@pytest.mark.parametrize("name", G.CHAIN_CASES)
+def test_chain_hf_warpers_keep_set(name):
+    c = G.case(name)
+    m = c["meta"]
+    r = oracle.run(G.chain_step(name, top_k=m["top_k"], top_p=m["top_p"], top_p_mode=N.TOPP_HF))
+    out, ref = r["out_scores"], c["final_hf"]
+    for row in range(out.shape[0]):
+        kg, kr = np.isfinite(out[row]), np.isfinite(ref[row])
+        if not np.array_equal(kg, kr):
+            assert G.explain_keep_mismatch(c["processed"][row], kr, kg, m["top_p"], int(r["out_status"][row])), row
+        else:
+            assert np.array_equal(out[row][kg], ref[row][kr])
+
+
+@pytest.mark.parametrize("name", G.CHAIN_CASES)
+def test_chain_sample_fn_keep_set(name):
+    # compiled_decode._sample: top-k then descending-cumsum top-p (shifted by one)
+    c = G.case(name)
+    m = c["meta"]
+    r = oracle.run(G.chain_step(name, top_k=m["top_k"], top_p=m["top_p"], top_p_mode=N.TOPP_SAMPLE_FN))
+    for row in range(r["out_scores"].shape[0]):
+        kg = np.isfinite(r["out_scores"][row])
+        kr = c["sample_fn_probs"][row] > 0
+        if not np.array_equal(kg, kr):
+            assert G.explain_keep_mismatch(c["processed"][row], kr, kg, m["top_p"], int(r["out_status"][row])), row
+
+
+@pytest.mark.parametrize("name", G.CHAIN_CASES)
+def test_chain_greedy_ids(name):
+    c = G.case(name)
+    r = oracle.run(G.chain_step(name, select_mode=N.SELECT_ARGMAX))
+    assert np.array_equal(r["out_ids"], c["greedy"].reshape(-1))
+
+
+def test_hf_repetition_penalty_then_warpers():
+    c = G.case("hf_repetition")
+    x = c["logits"]
+    s = G.StepInputs(logits=G.bf16_bits(x), dtype="bf16", num_rows=x.shape[0], input_ids=c["input_ids"],
+                     repetition_penalty=1.1, select_mode=N.SELECT_NONE, want_scores=True)
+    assert np.array_equal(oracle.run(s)["out_scores"], c["processed"])
+    r = oracle.run(s.with_(top_k=50, top_p=0.95))
+    out, ref = r["out_scores"], c["final_hf"]
+    for row in range(out.shape[0]):
+        kg, kr = np.isfinite(out[row]), np.isfinite(ref[row])
+        if not np.array_equal(kg, kr):
+            assert G.explain_keep_mismatch(c["processed"][row], kr, kg, 0.95, int(r["out_status"][row])), row
