@@ -59,6 +59,9 @@ def parse_args():
     p.add_argument("--e2e-steps", type=int, default=48)
     p.add_argument("--b64-steps", type=int, default=2048)
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--profile", type=int, default=0,
+                   help="only run this many eager launches of one workload (for ncu), print nothing")
+    p.add_argument("--profile-workload", choices=["sharded", "b64"], default="sharded")
     return p.parse_args()
 
 
@@ -237,6 +240,9 @@ def run_ours(args, dist: Dist):
     _native.load()  # fail loudly without the native library
     device = torch.device("cuda", dist.local)
     torch.cuda.set_device(device)
+    if args.profile and args.profile_workload == "b64":
+        run_b64(args, device, torch.cuda.Stream(device), dist, profile=args.profile)
+        return
     if PAIRS % dist.world:
         raise SystemExit(f"{PAIRS} pairs do not split over {dist.world} GPUs")
     pairs = PAIRS // dist.world
@@ -257,6 +263,12 @@ def run_ours(args, dist: Dist):
         for i in range(args.warmup):
             step(i)
     torch.cuda.synchronize()
+    if args.profile:
+        with torch.cuda.stream(stream):
+            for i in range(args.profile):
+                step(i)
+        torch.cuda.synchronize()
+        return
     with ClockSampler(device.index) as clocks:
         ms, graph = time_graph(step, args.steps, stream, dist)
     ms = dist.max(ms)
@@ -326,7 +338,7 @@ def run_ours(args, dist: Dist):
         print(json.dumps(line), flush=True)
 
 
-def run_b64(args, device, stream, dist):
+def run_b64(args, device, stream, dist, profile=0):
     """64 CFG pairs x V=4096 bf16, CFG + monotonic + grammar + T 0.9 on time shifts + top_p 0.9."""
     from mapperatorinator_b200.sampling import FusedSampler, GrammarTable
 
@@ -352,9 +364,11 @@ def run_b64(args, device, stream, dist):
         s.step(pool[i % nbuf], uniforms=u[i % nbuf])
 
     with torch.cuda.stream(stream):
-        for i in range(16):
+        for i in range(16 + profile):
             step(i)
     torch.cuda.synchronize()
+    if profile:
+        return None
     ms, g = time_graph(step, steps, stream, dist)
     del g
     return {"us_per_step": ms * 1e3 / steps, "steps": steps, "pairs": pairs,

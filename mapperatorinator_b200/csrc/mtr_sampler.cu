@@ -795,7 +795,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         hm = sm.hmass_m;
       }
       find_crossing(hm, lim - above, &sm.cr);
-      const int b = sm.cr.bin;
+      const int b = max(sm.cr.bin, 0);  // a crossing exists: above <= lim < above + candidates
       const uint32_t d = 255u - (uint32_t)b;
       prefix |= d << shift;
       mask |= 255u << shift;
@@ -876,7 +876,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         hc = sm.hcnt_m;
       }
       find_crossing(hc, lim, &sm.cr);
-      const int bstar = sm.cr.bin;
+      const int bstar = max(sm.cr.bin, 0);  // k - 1 < finite count, so a crossing exists
       const u64 c_above = sm.cr.above;
       const u64 n_c = sm.cr.w;
       if (n_c <= (u64)CAP && !force_radix) {
@@ -1023,7 +1023,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
           const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
           __syncthreads();
           find_crossing(hm, plim, &sm.cr);
-          const int bstar = sm.cr.bin;
+          const int bstar = max(sm.cr.bin, 0);  // plim < total since top_p < 1
           const u64 w_above = sm.cr.above;
 #pragma unroll
           for (int k = 0; k < EPT; ++k) {

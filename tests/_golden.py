@@ -82,10 +82,18 @@ def chain_step(name: str, *, select_mode=N.SELECT_NONE, top_k=0, top_p=1.0, top_
 
 
 def explain_keep_mismatch(scores: np.ndarray, ref_keep: np.ndarray, got_keep: np.ndarray, top_p: float,
-                          status: int, margin: float = 1e-5) -> bool:
+                          status: int | None = None, margin: float = 1e-5) -> bool:
     """True when a keep-set difference in one row is a tie at the cut or a
-    cumulative mass within `margin` of top_p (float64 reference mass)."""
-    if status & N.ROW_TIE_AT_CUT:
+    cumulative mass within `margin` of top_p (float64 reference mass).
+
+    With ``status`` None the tie is read from the data: every differing token
+    has the score of the smallest kept score."""
+    diff_ids = np.nonzero(ref_keep != got_keep)[0]
+    if status is None:
+        cut = min(scores[ref_keep].min(), scores[got_keep].min())
+        if (scores[diff_ids] == cut).all():
+            return True
+    elif status & N.ROW_TIE_AT_CUT:
         return True
     fin = np.isfinite(scores)
     x = scores[fin].astype(np.float64)
