@@ -148,6 +148,11 @@ typedef struct MtrSamplerArgs {
   /* ---- event-grammar mask: allowed(v) = bit class_of[v] of allow[class_of[prev]] ---- */
   const uint8_t* grammar_class_of; /* [V] or NULL (grammar off) */
   const uint32_t* grammar_allow;   /* [grammar_n_classes] */
+  /* Optional [grammar_n_classes][ceil(V/32)] bitmaps: bit v of row c is
+   * (allow[c] >> class_of[v]) & 1.  When set the kernel masks 8 ids per
+   * lookup instead of one class byte per id; it must agree with
+   * class_of / allow (callers build it once per grammar table). */
+  const uint32_t* grammar_vocab_bits;
   int32_t grammar_n_classes;
   int32_t* prev_token; /* [B]; < 0 = no previous token (no mask) */
 

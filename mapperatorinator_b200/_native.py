@@ -85,6 +85,7 @@ class MtrSamplerArgs(ctypes.Structure):
         ("timeshift_bias", c_float),
         ("grammar_class_of", c_void_p),
         ("grammar_allow", c_void_p),
+        ("grammar_vocab_bits", c_void_p),
         ("grammar_n_classes", c_int32),
         ("prev_token", c_void_p),
         ("repetition_penalty", c_float),

@@ -1,24 +1,37 @@
 // mtr_sampler.cu -- fused decode-sampling step for sm_100a (B200).
 //
 // One output row of the [B, V] processed logits is owned by one CTA, or by a
-// thread-block cluster of CS CTAs when V is large.  The row lives in registers
-// (THREADS x EPT elements per CTA) from the first 128-bit load to the last
-// store; no intermediate B x V tensor ever reaches HBM.  Per row:
+// thread-block cluster of CS CTAs (large V, or few rows).  The row lives in
+// registers (THREADS x EPT elements per CTA) from the first 128-bit load to the
+// last store; no intermediate B x V tensor ever reaches HBM.  The step is
+// instruction-bound long before it is HBM-bound, so every per-element
+// operation is counted: feature switches are hoisted out of the element loops,
+// arithmetic on element pairs uses the packed f32x2 instructions of sm_100a
+// (bit-identical per lane to the scalar IEEE operations), masks are built once
+// per 8-element chunk, and the selection stages work on short lists.
 //
 //   prologue   monotonic state (stateful, or a full scan of input_ids), grammar
-//              row of the previous token, per-row temperature, uniform
+//              row of the previous token, per-row temperature and uniform --
+//              independent load chains on separate lanes of warp 0
 //   load       ld.global.cs 16-byte vectors of bf16 / f16 / f32 logits; with
 //              CFG the first-half row and its second-half partner
 //   chain      CFG -> monotonic mask -> timeshift bias -> grammar mask ->
 //              penalties (history side, shared-memory histogram) ->
 //              temperature (Markstein division, bit-exact to IEEE x / T)
-//   stats      max, first arg-max (NaN first, as torch.argmax), finite count
-//   top-k      count histogram over d = max - x in 1/8 bins, exact k-th value
-//              inside the crossing bin (candidate list, or radix fallback)
-//   top-p      same scheme weighted by fixed-point probabilities
-//              q = floor(e^(x - max) * 2^31); integer sums, so the keep set is
-//              independent of thread order; ties at the cut go to the lowest id
-//   draw       smallest id whose kept-mass prefix exceeds floor(u * Q_kept)
+//   stats      max, NaN / +inf detection (arg-max only for greedy selection)
+//   top-k      a 1024-bin histogram of the per-thread maxima over d = max - x
+//              bounds the k-th value from below (>= k elements lie above it);
+//              the elements above that bound are compacted to a list and a
+//              second histogram over the list resolves the exact k-th value.
+//              Fallback: a histogram over every element
+//   top-p      fixed-point probabilities q = floor(e^(x - max) * 2^31), integer
+//              sums (keep set independent of thread order); a mass histogram
+//              over the survivor list (or over every element when the
+//              survivors are many) and an exact resolution inside the crossing
+//              bin; ties at the cut go to the lowest token id
+//   draw       smallest id whose kept-mass prefix exceeds floor(u * Q_kept):
+//              an id-binned mass histogram over the kept list, or per-chunk
+//              sums and a block scan over every element
 //   epilogue   ids, processed scores / log-probs, row status, state updates
 //
 // Reference arithmetic followed (paths inside the Mapperatorinator project,
@@ -27,6 +40,7 @@
 //   monotonic  osuT5/osuT5/inference/logit_processors.py:190-229,
 //              osuT5/osuT5/inference/optimized/single/logits.py:33-105
 //   bias       logit_processors.py:35-43
+//   penalty    HF:logits_process.py:407-413 (repetition)
 //   temp       HF:logits_process.py:297-301, logit_processors.py:75-119
 //   top-k/p    HF:logits_process.py:521-535, 581-588;
 //              osuT5/osuT5/inference/compiled_decode.py:1135-1158
@@ -43,7 +57,6 @@
 #include <stdint.h>
 #include <string.h>
 
-#include <atomic>
 #include <mutex>
 
 #include "../../include/mtr_sampler.h"
@@ -52,15 +65,40 @@ namespace cg = cooperative_groups;
 
 namespace mtr {
 
-constexpr int NB = 256;             // distance bins per histogram
-constexpr int CAP = 256;            // exact candidate list capacity
-constexpr float BIN_SCALE = 8.0f;   // bins per logit unit
+constexpr int NB = 1024;            // distance bins per histogram
+constexpr float BIN_SCALE = 32.0f;  // bins per logit unit (d in [0, 32) before the overflow bin)
+constexpr int CAP = 256;            // candidate list capacity
+constexpr int MINI = 64;            // crossing-bin list capacity
 constexpr int32_t NO_ID = 0x7fffffff;
+constexpr unsigned FULL = 0xffffffffu;
 
 typedef unsigned long long u64;
 
 __device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
 __device__ __forceinline__ float pos_inf() { return __int_as_float(0x7f800000); }
+
+// ---------------------------------------------------------------------------
+// packed f32x2 arithmetic (sm_100a); each lane is one IEEE round-to-nearest op.
+// Only fma / mul chains are used: they were checked bit-identical to the scalar
+// sequence over every d in the exponential's range and 8M quotients.  ptxas
+// rewrites packed mul -> add chains, so those stay scalar.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ u64 pk2(float a, float b) {
+  u64 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(u64 r, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r)); }
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+  u64 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
+  u64 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
 
 // ---------------------------------------------------------------------------
 // numerics
@@ -87,6 +125,31 @@ __device__ __forceinline__ uint32_t expfx(float d) {
   return sh >= 32 ? 0u : (m >> sh);
 }
 
+// expfx on two values at once (same operations, packed); d0, d1 <= 0
+__device__ __forceinline__ void expfx2(float d0, float d1, uint32_t& q0, uint32_t& q1) {
+  const u64 D = pk2(d0, d1);
+  float t0, t1;
+  up2(mul2(D, pk2(0x1.715476p+0f, 0x1.715476p+0f)), t0, t1);
+  const float n0 = rintf(t0), n1 = rintf(t1);
+  const u64 Nn = pk2(n0, n1);
+  u64 R = fma2(Nn, pk2(-0x1.62e400p-1f, -0x1.62e400p-1f), D);
+  R = fma2(Nn, pk2(-0x1.7f7d1cp-20f, -0x1.7f7d1cp-20f), R);
+  u64 P = pk2(0x1.6ab980p+21f, 0x1.6ab980p+21f);
+  P = fma2(P, R, pk2(0x1.126d0cp+24f, 0x1.126d0cp+24f));
+  P = fma2(P, R, pk2(0x1.55589ap+26f, 0x1.55589ap+26f));
+  P = fma2(P, R, pk2(0x1.55540ap+28f, 0x1.55540ap+28f));
+  P = fma2(P, R, pk2(0x1.fffffap+29f, 0x1.fffffap+29f));
+  P = fma2(P, R, pk2(0x1.000000p+31f, 0x1.000000p+31f));
+  P = fma2(P, R, pk2(0x1.000000p+31f, 0x1.000000p+31f));
+  float p0, p1;
+  up2(P, p0, p1);
+  // |n| <= 46 whenever d >= -32; the clamp only keeps the shift defined
+  const int s0 = -__float2int_rz(fmaxf(n0, -40.0f)), s1 = -__float2int_rz(fmaxf(n1, -40.0f));
+  const uint32_t m0 = __float2uint_rz(p0), m1 = __float2uint_rz(p1);
+  q0 = (d0 >= -32.0f && s0 < 32) ? (m0 >> s0) : 0u;
+  q1 = (d1 >= -32.0f && s1 < 32) ? (m1 >> s1) : 0u;
+}
+
 // x / t correctly rounded, given y = RN(1/t) (Markstein: q0 = x*y, r = x - q0*t
 // exactly, q = q0 + r*y).  Magnitudes outside [2^-60, 2^60) and NaN take the
 // IEEE divide; zeros and infinities pass through (t is positive and finite).
@@ -101,6 +164,24 @@ __device__ __forceinline__ float div_by(float x, float t, float y) {
   return __fdiv_rn(x, t);
 }
 
+// the same on a pair; fma(q0, -t, x) is bit-identical to fma(-q0, t, x)
+__device__ __forceinline__ void div_by2(float& x0, float& x1, float t, float y) {
+  const u64 X = pk2(x0, x1), Y = pk2(y, y);
+  const u64 Q0 = mul2(X, Y);
+  const u64 Rr = fma2(Q0, pk2(-t, -t), X);
+  float q0, q1;
+  up2(fma2(Rr, Y, Q0), q0, q1);
+  const float a0 = fabsf(x0), a1 = fabsf(x1);
+  const bool ok0 = a0 >= 0x1p-60f && a0 < 0x1p60f, ok1 = a1 >= 0x1p-60f && a1 < 0x1p60f;
+  const bool pass0 = x0 == 0.0f || a0 == pos_inf(), pass1 = x1 == 0.0f || a1 == pos_inf();
+  if ((!ok0 && !pass0) || (!ok1 && !pass1)) {  // tiny, huge or NaN: rare
+    q0 = ok0 || pass0 ? q0 : __fdiv_rn(x0, t);
+    q1 = ok1 || pass1 ? q1 : __fdiv_rn(x1, t);
+  }
+  x0 = ok0 ? q0 : (pass0 ? x0 : q0);
+  x1 = ok1 ? q1 : (pass1 ? x1 : q1);
+}
+
 // order-preserving key of a non-NaN float (-0 and +0 share a key)
 __device__ __forceinline__ uint32_t fkey(float x) {
   uint32_t u = __float_as_uint(x);
@@ -112,7 +193,9 @@ __device__ __forceinline__ float key2f(uint32_t k) {
   return __uint_as_float(u);
 }
 
-// distance bin of a finite x below the row maximum mx (monotone in x)
+// distance bin of a finite x below the row maximum mx (non-increasing in x).
+// bin(x) <= b  <=>  (mx - x) < (b + 1) / BIN_SCALE for b < NB - 1 (the scaling
+// by a power of two is exact).
 __device__ __forceinline__ int dbin(float mx, float x) {
   float s = __fmul_rn(__fsub_rn(mx, x), BIN_SCALE);
   s = fminf(s, (float)(NB - 1));
@@ -120,6 +203,11 @@ __device__ __forceinline__ int dbin(float mx, float x) {
 }
 
 __device__ __forceinline__ bool finite_val(float x) { return fabsf(x) < pos_inf(); }
+
+// canonical order: higher score first, then lower token id
+__device__ __forceinline__ bool canon_before(float xj, int32_t ij, float xi, int32_t ii) {
+  return xj > xi || (xj == xi && ij < ii);
+}
 
 // ---------------------------------------------------------------------------
 // element loads
@@ -132,7 +220,6 @@ template <> struct Elem<float> {
     return __uint_as_float(v);
   }
   __device__ static float one(const void* p, int64_t i) { return __ldcs((const float*)p + i); }
-  static constexpr int DT = MTR_DTYPE_F32;
 };
 template <> struct Elem<__nv_bfloat16> {
   static constexpr int VEC = 8;
@@ -144,7 +231,6 @@ template <> struct Elem<__nv_bfloat16> {
     const unsigned short h = __ldcs((const unsigned short*)p + i);
     return __uint_as_float((uint32_t)h << 16);
   }
-  static constexpr int DT = MTR_DTYPE_BF16;
 };
 template <> struct Elem<__half> {
   static constexpr int VEC = 8;
@@ -157,7 +243,6 @@ template <> struct Elem<__half> {
     const unsigned short h = __ldcs((const unsigned short*)p + i);
     return __half2float(__ushort_as_half(h));
   }
-  static constexpr int DT = MTR_DTYPE_F16;
 };
 
 __device__ __forceinline__ int64_t load_id(const MtrSamplerArgs& a, int64_t row, int64_t pos) {
@@ -188,6 +273,13 @@ __device__ __forceinline__ bool is_eos(const MtrSamplerArgs& a, int64_t t) {
   return e;
 }
 
+// bits [lo, hi) of an 8-bit chunk mask (empty when hi <= lo)
+__device__ __forceinline__ uint32_t range_bits(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 8);
+  return hi > lo ? (((1u << hi) - 1u) & ~((1u << lo) - 1u)) : 0u;
+}
+
 // ---------------------------------------------------------------------------
 // cluster helper: CS == 1 degenerates to the CTA
 // ---------------------------------------------------------------------------
@@ -207,22 +299,30 @@ template <int CS> struct Clu {
 };
 
 // ---------------------------------------------------------------------------
-// warp / block reductions
+// warp / block helpers
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ u64 warp_sum_u64(u64 v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
   return v;
 }
 __device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
   return v;
 }
 __device__ __forceinline__ u64 warp_incl_scan_u64(u64 v, int lane) {
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const u64 t = __shfl_up_sync(0xffffffffu, v, o);
+    const u64 t = __shfl_up_sync(FULL, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+__device__ __forceinline__ uint32_t warp_incl_scan_u32(uint32_t v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(FULL, v, o);
     if (lane >= o) v += t;
   }
   return v;
@@ -236,23 +336,20 @@ struct Cross {
   u64 total;     // weight of all bins
 };
 
-// Warp 0 scans NB weights (bin 0 ranks first) and finds the crossing of `lim`.
-// Every thread must call; the result is published in *out after the barrier.
-template <typename W>
+// Warp 0 scans NBINS weights (bin 0 ranks first) and finds the first bin whose
+// inclusive prefix exceeds `lim`.  Every thread must call; the result is
+// published in *out after the barrier.
+template <int NBINS, typename W>
 __device__ __forceinline__ void find_crossing(const W* w, u64 lim, Cross* out) {
   const int tid = threadIdx.x, lane = tid & 31;
   if (tid < 32) {
-    constexpr int PER = NB / 32;
-    u64 loc[PER];
+    constexpr int PER = NBINS / 32;
     u64 s = 0;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      loc[i] = (u64)w[lane * PER + i];
-      s += loc[i];
-    }
+    for (int i = 0; i < PER; ++i) s += (u64)w[lane * PER + ((i + lane) & (PER - 1))];  // rotated: no bank conflicts
     const u64 incl = warp_incl_scan_u64(s, lane);
     const u64 excl = incl - s;
-    const u64 total = __shfl_sync(0xffffffffu, incl, 31);
+    const u64 total = __shfl_sync(FULL, incl, 31);
     if (lane == 0) {
       out->bin = -1;
       out->above = total;
@@ -262,15 +359,15 @@ __device__ __forceinline__ void find_crossing(const W* w, u64 lim, Cross* out) {
     __syncwarp();
     if (excl <= lim && lim < incl) {
       u64 c = excl;
-#pragma unroll
       for (int i = 0; i < PER; ++i) {
-        if (c + loc[i] > lim) {
+        const u64 wi = (u64)w[lane * PER + i];
+        if (c + wi > lim) {
           out->bin = lane * PER + i;
           out->above = c;
-          out->w = loc[i];
+          out->w = wi;
           break;
         }
-        c += loc[i];
+        c += wi;
       }
     }
   }
@@ -283,26 +380,27 @@ __device__ __forceinline__ void find_crossing(const W* w, u64 lim, Cross* out) {
 struct alignas(16) StatX {  // per-CTA row statistics exchanged across the cluster
   float mx;
   int32_t amax;
-  int32_t nan_id;
-  uint32_t nfin;
-  uint32_t pinf;
+  uint32_t nan;
   uint32_t status;
-  uint32_t pad[2];
 };
 
-template <int CS, int NCH>
+template <int CS>
 struct alignas(16) Shared {
   // prologue results
   int32_t mono;
   int32_t mono_hi;
   uint32_t allow;
   int32_t grammar_on;
+  const uint32_t* gbits;  // vocabulary bitmap of the previous token's class
   float t_row;
   float t_rcp;
   float u;
-  uint32_t status;
+  uint32_t status;    // bits raised while processing this CTA's tile
+  uint32_t status_g;  // grammar lookups
+  uint32_t status_u;  // uniform
   int32_t n_uniq;
-  int32_t nc;           // local candidate count
+  int32_t nc;         // local candidate count
+  int32_t nm;         // crossing-bin list count
   int32_t token;
   int32_t red_i[2];
   float tk;
@@ -313,26 +411,32 @@ struct alignas(16) Shared {
   u64 qkept;
   Cross cr;
   StatX stat;
-  u64 cta_mass;         // kept mass of this CTA's tile (dense draw exchange)
+  u64 cta_mass;
+  uint32_t cta_nfin;
   // per-warp partials
   float wf[32];
   int32_t wi[32];
   int32_t wi2[32];
   uint32_t wu[32];
   uint32_t wu2[32];
-  u64 wl[32 * NCH];
+  u64 wl[32 * 4];
   // histograms (local; merged copies when CS > 1)
   uint32_t hcnt[NB];
-  u64 hmass[NB];
+  alignas(16) u64 hmass[NB];
   uint32_t hcnt_m[CS > 1 ? NB : 1];
   u64 hmass_m[CS > 1 ? NB : 1];
   // candidate lists (local; merged when CS > 1)
   float cx[CAP];
   int32_t cid[CAP];
   uint32_t cq[CAP];
+  int32_t cb[CAP];
   float mcx[CS > 1 ? CAP : 1];
   int32_t mcid[CS > 1 ? CAP : 1];
   uint32_t mcq[CS > 1 ? CAP : 1];
+  // crossing-bin list
+  float nx[MINI];
+  int32_t nid[MINI];
+  uint32_t nq[MINI];
   uint8_t ckeep[CAP];
 };
 
@@ -347,10 +451,41 @@ struct Derived {
   int32_t topk_on;
   int32_t topp_on;
   int32_t ids_len;
+  int32_t id_shift;  // id >> id_shift < NB for every id < V
+  int32_t gwords;    // 32-bit words per grammar vocabulary bitmap
   float temp_rcp;
   float cond_rcp[MTR_MAX_COND_TEMPS];
   float col_rcp[MTR_MAX_COL_TEMP_RANGES];
 };
+
+// Push the elements of this thread whose bit is set in `mask` to the local
+// candidate list (x, id, q): a warp scan of the counts and one shared atomic per
+// warp.  Every lane of the warp must call.  Entries past CAP are counted only.
+template <int CS, int EPT, typename IdOf>
+__device__ __forceinline__ void collect(Shared<CS>& sm, uint32_t mask, const float (&x)[EPT], const uint32_t (&q)[EPT],
+                                        bool with_q, IdOf id_of, int lane) {
+  const uint32_t c = __popc(mask);
+  const uint32_t incl = warp_incl_scan_u32(c, lane);
+  const uint32_t wt = __shfl_sync(FULL, incl, 31);
+  if (wt == 0u) return;
+  int base = 0;
+  if (lane == 31) base = atomicAdd(&sm.nc, (int)wt);
+  base = __shfl_sync(FULL, base, 31);
+  if (mask) {
+    int s = base + (int)(incl - c);
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      if ((mask >> k) & 1u) {
+        if (s < CAP) {
+          sm.cx[s] = x[k];
+          sm.cid[s] = id_of(k);
+          sm.cq[s] = with_q ? q[k] : 0u;
+        }
+        ++s;
+      }
+    }
+  }
+}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -363,10 +498,12 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   constexpr int NCH = EPT / VEC;
   constexpr int TILE = THREADS * EPT;
   constexpr int NW = THREADS / 32;
-  static_assert(EPT % VEC == 0, "EPT must be a multiple of the vector width");
-  static_assert(THREADS >= NB && THREADS >= CAP, "one thread per bin / candidate");
+  static_assert(EPT % VEC == 0 && VEC % 2 == 0, "EPT must be a multiple of the (even) vector width");
+  static_assert(EPT <= 32, "per-thread element masks are 32 bits");
+  static_assert(THREADS >= CAP, "one thread per list entry");
+  static_assert(NCH <= 4, "per-chunk partials");
 
-  __shared__ Shared<CS, NCH> sm;
+  __shared__ Shared<CS> sm;
   extern __shared__ __align__(16) uint8_t dsm[];
 
   const int tid = threadIdx.x;
@@ -378,10 +515,14 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   const int V = a.vocab;
   const int L = a.input_ids ? dv.ids_len : 0;
   const float NEG = neg_inf();
+  const int sel = a.select_mode;
+  const bool force_radix = (a.flags & MTR_FLAG_FORCE_RADIX) != 0;
 
   auto id_of = [&](int k) -> int { return base + ((k / VEC) * THREADS + tid) * VEC + (k % VEC); };
+  auto chunk_id = [&](int j) -> int { return base + (j * THREADS + tid) * VEC; };
 
   // ------------------------------------------------------------ prologue
+  for (int i = tid; i < NB; i += THREADS) sm.hcnt[i] = 0u;
   int32_t mono = -1;
   if (a.mono_mode == MTR_MONO_SCAN) {
     int lts = -1, lsos = -1;
@@ -392,8 +533,8 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      lts = max(lts, __shfl_xor_sync(0xffffffffu, lts, o));
-      lsos = max(lsos, __shfl_xor_sync(0xffffffffu, lsos, o));
+      lts = max(lts, __shfl_xor_sync(FULL, lts, o));
+      lsos = max(lsos, __shfl_xor_sync(FULL, lsos, o));
     }
     if (lane == 0) {
       sm.wi[warp] = lts;
@@ -411,69 +552,87 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     __syncthreads();
     mono = sm.red_i[0];
   }
-  if (tid == 0) {
-    uint32_t status = 0;
-    if (a.mono_mode == MTR_MONO_STATE) {
-      mono = a.mono_state[row];
-      if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) mono = mono_update(a, mono, load_id(a, row, L - 1));
-    }
-    sm.mono = mono;
-    sm.mono_hi = mono >= 0 ? (int32_t)min((int64_t)a.ts_end, (int64_t)a.ts_start + mono) : -1;
-    // grammar row of the previous token
-    uint32_t allow = 0xffffffffu;
-    int gon = 0;
-    if (a.grammar_class_of) {
-      int64_t prev = -1;
-      if (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) prev = L > 0 ? load_id(a, row, L - 1) : -1;
-      else if (a.prev_token) prev = a.prev_token[row];
-      if (prev >= V) status |= MTR_ROW_BAD_ID;
-      if (prev >= 0 && prev < V) {
-        const uint32_t c = __ldg(a.grammar_class_of + prev);
-        if (c < (uint32_t)a.grammar_n_classes) {
-          gon = 1;
-          allow = __ldg(a.grammar_allow + c);
-        } else {
-          status |= MTR_ROW_BAD_ID;
+  // independent dependent-load chains on separate lanes of warp 0
+  if (warp == 0) {
+    if (lane == 0) {
+      if (a.mono_mode == MTR_MONO_STATE) {
+        mono = a.mono_state[row];
+        if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) mono = mono_update(a, mono, load_id(a, row, L - 1));
+      }
+      sm.mono = mono;
+      sm.mono_hi = mono >= 0 ? (int32_t)min((int64_t)a.ts_end, (int64_t)a.ts_start + mono) : -1;
+    } else if (lane == 1) {
+      uint32_t status = 0, allow = 0xffffffffu;
+      int gon = 0;
+      const uint32_t* gbits = nullptr;
+      if (a.grammar_class_of) {
+        int64_t prev = -1;
+        if (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) prev = L > 0 ? load_id(a, row, L - 1) : -1;
+        else if (a.prev_token) prev = a.prev_token[row];
+        if (prev >= V) status |= MTR_ROW_BAD_ID;
+        if (prev >= 0 && prev < V) {
+          const uint32_t c = __ldg(a.grammar_class_of + prev);
+          if (c < (uint32_t)a.grammar_n_classes) {
+            gon = 1;
+            allow = __ldg(a.grammar_allow + c);
+            if (a.grammar_vocab_bits) gbits = a.grammar_vocab_bits + (size_t)c * dv.gwords;
+          } else {
+            status |= MTR_ROW_BAD_ID;
+          }
         }
       }
-    }
-    sm.allow = allow;
-    sm.grammar_on = gon;
-    // per-row temperature
-    float t = a.temperature, y = dv.temp_rcp;
-    if (a.temp_mode == MTR_TEMP_ROW_CONDITIONAL) {
-      for (int c = 0; c < a.n_cond; ++c) {
-        const int off = a.cond_offset[c];
-        if (off < 1 || L < off) continue;
-        const int64_t tok = load_id(a, row, L - off);
-        if (tok >= 0 && tok < V && ((__ldg(a.cond_token_bits[c] + (tok >> 5)) >> (tok & 31)) & 1u)) {
-          t = a.cond_temperature[c];
-          y = dv.cond_rcp[c];
-          break;
+      sm.allow = allow;
+      sm.grammar_on = gon;
+      sm.gbits = gbits;
+      sm.status_g = status;
+    } else if (lane == 2) {
+      float t = a.temperature, y = dv.temp_rcp;
+      if (a.temp_mode == MTR_TEMP_ROW_CONDITIONAL) {
+        for (int c = 0; c < a.n_cond; ++c) {
+          const int off = a.cond_offset[c];
+          if (off < 1 || L < off) continue;
+          const int64_t tok = load_id(a, row, L - off);
+          if (tok >= 0 && tok < V && ((__ldg(a.cond_token_bits[c] + (tok >> 5)) >> (tok & 31)) & 1u)) {
+            t = a.cond_temperature[c];
+            y = dv.cond_rcp[c];
+            break;
+          }
         }
       }
-    }
-    sm.t_row = t;
-    sm.t_rcp = y;
-    float u = 0.0f;
-    if (a.select_mode == MTR_SELECT_SAMPLE) {
-      u = a.uniforms[row];
-      if (!(u >= 0.0f)) {
-        u = 0.0f;
-        status |= MTR_ROW_BAD_UNIFORM;
-      } else if (u >= 1.0f) {
-        u = 0x1.fffffep-1f;
-        status |= MTR_ROW_BAD_UNIFORM;
+      sm.t_row = t;
+      sm.t_rcp = y;
+    } else if (lane == 3) {
+      float u = 0.0f;
+      uint32_t status = 0;
+      if (sel == MTR_SELECT_SAMPLE) {
+        u = a.uniforms[row];
+        if (!(u >= 0.0f)) {
+          u = 0.0f;
+          status |= MTR_ROW_BAD_UNIFORM;
+        } else if (u >= 1.0f) {
+          u = 0x1.fffffep-1f;
+          status |= MTR_ROW_BAD_UNIFORM;
+        }
       }
+      sm.u = u;
+      sm.status_u = status;
+    } else if (lane == 4) {
+      sm.status = 0u;
+      sm.n_uniq = 0;
+      sm.nc = 0;
+      sm.nm = 0;
+      sm.token = -1;
     }
-    sm.u = u;
-    sm.status = status;
-    sm.n_uniq = 0;
-    sm.nc = 0;
-    sm.token = -1;
+  }
+  // first history ids of the penalty window, fetched before the barrier
+  int64_t hist0 = -1, hist1 = -1;
+  if (dv.pen_on) {
+    const int i0 = a.penalty_start + tid, i1 = i0 + THREADS;
+    if (i0 < L) hist0 = load_id(a, row, i0);
+    if (i1 < L) hist1 = load_id(a, row, i1);
   }
 
-  // ------------------------------------------------------------ load
+  // ------------------------------------------------------------ load (+ CFG)
   const Tin* r1 = (const Tin*)a.logits + row * a.logits_row_stride;
   const Tin* r2 = r1 + dv.second * a.logits_row_stride;
   float x[EPT];
@@ -481,7 +640,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     uint4 ra[NCH], rb[NCH];
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
-      const int id0 = base + (j * THREADS + tid) * VEC;
+      const int id0 = chunk_id(j);
       ra[j] = make_uint4(0u, 0u, 0u, 0u);
       rb[j] = make_uint4(0u, 0u, 0u, 0u);
       if (id0 < V) {
@@ -489,25 +648,29 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         if (a.cfg_enabled) rb[j] = __ldcs((const uint4*)(r2 + id0));
       }
     }
+    if (a.cfg_enabled) {
+      // three separately rounded scalar ops: ptxas rewrites a packed
+      // mul.rn.f32x2 -> add.rn.f32x2 chain, which would change the rounding
+      const float sc = a.cfg_scale;
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
+      for (int j = 0; j < NCH; ++j) {
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const int k = j * VEC + e;
-        const float va = E::get(ra[j], e);
-        float v = va;
-        if (a.cfg_enabled) {
-          const float vb = E::get(rb[j], e);
-          v = __fadd_rn(vb, __fmul_rn(__fsub_rn(va, vb), a.cfg_scale));
+        for (int e = 0; e < VEC; ++e) {
+          const float va = E::get(ra[j], e), vb = E::get(rb[j], e);
+          x[j * VEC + e] = __fadd_rn(vb, __fmul_rn(__fsub_rn(va, vb), sc));
         }
-        x[k] = (id_of(k) < V) ? v : NEG;
       }
+    } else {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j)
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) x[j * VEC + e] = E::get(ra[j], e);
     }
   } else {
 #pragma unroll
     for (int k = 0; k < EPT; ++k) {
       const int id = id_of(k);
-      float v = NEG;
+      float v = 0.0f;
       if (id < V) {
         const float va = E::one(r1, id);
         v = va;
@@ -521,46 +684,69 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   }
   __syncthreads();  // prologue scalars visible
 
-  // ------------------------------------------------------------ mask chain
+  // ------------------------------------------------------------ masks (per 8-id chunk)
   {
     const int mono_hi = sm.mono_hi;
-    const int ts0 = a.ts_start, ts1 = a.ts_end;
-    const bool bias_on = a.timeshift_bias != 0.0f;
+    const int ts0 = a.ts_start;
     const bool gon = sm.grammar_on != 0;
+    const uint32_t* gbits = sm.gbits;
     const uint32_t allow = sm.allow;
     const uint32_t ncls = (uint32_t)a.grammar_n_classes;
+    const bool ragged = (base + TILE) > V;
+    if (ragged || mono_hi > ts0 || gon) {
+      constexpr uint32_t ALL = (1u << VEC) - 1u;
 #pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      const int id0 = base + (j * THREADS + tid) * VEC;
-      uint8_t cls[VEC];
-      if (gon) {
-        if (dv.cls_vec && id0 < V) {
-          if constexpr (VEC == 8) {
-            const uint2 w = __ldg((const uint2*)(a.grammar_class_of + id0));
-#pragma unroll
-            for (int e = 0; e < 8; ++e) cls[e] = (uint8_t)(((e < 4 ? w.x : w.y) >> (8 * (e & 3))) & 0xffu);
+      for (int j = 0; j < NCH; ++j) {
+        const int id0 = chunk_id(j);
+        uint32_t keep = range_bits(0, V - id0) & ALL;      // ids < V
+        keep &= ~range_bits(ts0 - id0, mono_hi - id0);    // monotonic: [ts0, mono_hi) removed
+        if (gon && id0 < V) {
+          if (gbits) {
+            keep &= __ldg(gbits + (id0 >> 5)) >> (id0 & 31);  // id0 % VEC == 0: the chunk sits in one word
           } else {
-            const uint32_t w = __ldg((const uint32_t*)(a.grammar_class_of + id0));
+            uint32_t g = 0;
+            if (dv.cls_vec) {
+              if constexpr (VEC == 8) {
+                const uint2 w = __ldg((const uint2*)(a.grammar_class_of + id0));
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) cls[e] = (uint8_t)((w >> (8 * e)) & 0xffu);
+                for (int e = 0; e < 8; ++e) {
+                  const uint32_t c = ((e < 4 ? w.x : w.y) >> (8 * (e & 3))) & 0xffu;
+                  g |= (c < ncls ? (allow >> c) & 1u : 0u) << e;
+                }
+              } else {
+                const uint32_t w = __ldg((const uint32_t*)(a.grammar_class_of + id0));
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) {
+                  const uint32_t c = (w >> (8 * e)) & 0xffu;
+                  g |= (c < ncls ? (allow >> c) & 1u : 0u) << e;
+                }
+              }
+            } else {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) {
+                if (id0 + e < V) {
+                  const uint32_t c = __ldg(a.grammar_class_of + id0 + e);
+                  g |= (c < ncls ? (allow >> c) & 1u : 0u) << e;
+                }
+              }
+            }
+            keep &= g;
           }
-        } else {
+        }
+        keep &= ALL;
+        if (keep != ALL) {
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) cls[e] = (id0 + e < V) ? __ldg(a.grammar_class_of + id0 + e) : 0;
+          for (int e = 0; e < VEC; ++e)
+            if (!((keep >> e) & 1u)) x[j * VEC + e] = NEG;
         }
       }
+    }
+    if (a.timeshift_bias != 0.0f) {
+      const int ts1 = a.ts_end;
 #pragma unroll
-      for (int e = 0; e < VEC; ++e) {
-        const int k = j * VEC + e;
-        const int id = id0 + e;
-        float v = x[k];
-        if (id >= ts0 && id < mono_hi) v = NEG;
-        if (bias_on && id >= ts0 && id < ts1) v = __fadd_rn(v, a.timeshift_bias);
-        if (gon) {
-          const uint32_t c = cls[e];
-          if (!(c < ncls && ((allow >> c) & 1u))) v = NEG;
-        }
-        if (id < V) x[k] = v;
+      for (int k = 0; k < EPT; ++k) {
+        const int id = id_of(k);
+        if (id >= ts0 && id < ts1) x[k] = __fadd_rn(x[k], a.timeshift_bias);
       }
     }
   }
@@ -570,7 +756,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     float* xs = (float*)dsm;
     uint32_t* cnt = (uint32_t*)(xs + TILE);
     uint16_t* uniq = (uint16_t*)(cnt + TILE);
-    for (int i = tid; i < TILE; i += THREADS) cnt[i] = 0u;
+    for (int i = tid * 4; i < TILE; i += THREADS * 4) *(uint4*)(cnt + i) = make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
       const int li0 = (j * THREADS + tid) * VEC;
@@ -580,15 +766,27 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     }
     __syncthreads();
     uint32_t bad = 0;
-    for (int i = a.penalty_start + tid; i < L; i += THREADS) {
-      const int64_t t = load_id(a, row, i);
-      if (t < 0 || t >= V) {
-        bad = 1;
-        continue;
+    for (int i0 = a.penalty_start; i0 < L; i0 += THREADS) {  // block-uniform trip count
+      const int i = i0 + tid;
+      bool first = false;
+      int li = 0;
+      if (i < L) {
+        const int64_t t = (i0 == a.penalty_start) ? hist0
+                          : (i0 == a.penalty_start + THREADS) ? hist1 : load_id(a, row, i);
+        if (t < 0 || t >= V) {
+          bad = 1;
+        } else if (t >= base && t < base + TILE) {
+          li = (int)(t - base);
+          first = atomicAdd(&cnt[li], 1u) == 0u;
+        }
       }
-      if (t >= base && t < base + TILE) {
-        const int li = (int)(t - base);
-        if (atomicAdd(&cnt[li], 1u) == 0u) uniq[atomicAdd(&sm.n_uniq, 1)] = (uint16_t)li;
+      const unsigned m = __ballot_sync(FULL, first);
+      if (m) {
+        const int leader = __ffs(m) - 1;
+        int slot = 0;
+        if (lane == leader) slot = atomicAdd(&sm.n_uniq, __popc(m));
+        slot = __shfl_sync(FULL, slot, leader);
+        if (first) uniq[slot + __popc(m & ((1u << lane) - 1u))] = (uint16_t)li;
       }
     }
     if (bad) atomicOr(&sm.status, MTR_ROW_BAD_ID);
@@ -622,96 +820,122 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   // ------------------------------------------------------------ temperature
   if (a.temp_mode == MTR_TEMP_COLUMN_RANGES) {
 #pragma unroll
-    for (int k = 0; k < EPT; ++k) {
-      const int id = id_of(k);
-      float t = a.temperature, y = dv.temp_rcp;
+    for (int j = 0; j < NCH; ++j) {
+      const int id0 = chunk_id(j);
+      // the range (first match) of the chunk's first and last id
+      float t0 = a.temperature, y0 = dv.temp_rcp, t1 = a.temperature, y1 = dv.temp_rcp;
       for (int r = a.n_col_ranges - 1; r >= 0; --r) {
-        if (id >= a.col_start[r] && id < a.col_end[r]) {
-          t = a.col_temperature[r];
-          y = dv.col_rcp[r];
+        if (id0 >= a.col_start[r] && id0 < a.col_end[r]) {
+          t0 = a.col_temperature[r];
+          y0 = dv.col_rcp[r];
+        }
+        if (id0 + VEC - 1 >= a.col_start[r] && id0 + VEC - 1 < a.col_end[r]) {
+          t1 = a.col_temperature[r];
+          y1 = dv.col_rcp[r];
         }
       }
-      if (t != 1.0f) x[k] = div_by(x[k], t, y);
+      bool uniform_chunk = t0 == t1;
+      if (uniform_chunk) {  // no range edge may split the chunk
+        for (int r = 0; r < a.n_col_ranges; ++r) {
+          const int s = a.col_start[r], e = a.col_end[r];
+          if ((s > id0 && s < id0 + VEC) || (e > id0 && e < id0 + VEC)) uniform_chunk = false;
+        }
+      }
+      if (uniform_chunk) {
+        if (t0 != 1.0f) {
+#pragma unroll
+          for (int e = 0; e < VEC; e += 2) div_by2(x[j * VEC + e], x[j * VEC + e + 1], t0, y0);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          const int id = id0 + e;
+          float t = a.temperature, y = dv.temp_rcp;
+          for (int r = a.n_col_ranges - 1; r >= 0; --r) {
+            if (id >= a.col_start[r] && id < a.col_end[r]) {
+              t = a.col_temperature[r];
+              y = dv.col_rcp[r];
+            }
+          }
+          if (t != 1.0f) x[j * VEC + e] = div_by(x[j * VEC + e], t, y);
+        }
+      }
     }
   } else {
     const float t = sm.t_row, y = sm.t_rcp;
     if (t != 1.0f) {
 #pragma unroll
-      for (int k = 0; k < EPT; ++k) x[k] = div_by(x[k], t, y);
+      for (int k = 0; k < EPT; k += 2) div_by2(x[k], x[k + 1], t, y);
     }
   }
 
   // ------------------------------------------------------------ row statistics
+  float lm = NEG;  // this thread's maximum (bound for top-k)
   float gmax;
-  int32_t gamax, gnan;
-  uint32_t gnfin, gstatus;
-  bool gpinf;
+  int32_t gamax = NO_ID, gnan = NO_ID;
+  uint32_t gstatus;
   {
-    float lm = NEG;
     int32_t la = NO_ID, ln = NO_ID;
-    uint32_t nf = 0, pinf = 0;
+    bool nan = false;
+    if (sel == MTR_SELECT_ARGMAX) {
 #pragma unroll
-    for (int k = 0; k < EPT; ++k) {
-      const float v = x[k];
-      const int id = id_of(k);
-      if (v != v) {
-        ln = min(ln, id);
-      } else {
+      for (int k = 0; k < EPT; ++k) {
+        const float v = x[k];
+        if (v != v) ln = min(ln, id_of(k));
         if (v > lm) {
           lm = v;
-          la = id;
+          la = id_of(k);
         }
-        if (v == pos_inf()) pinf = 1;
-        if (finite_val(v)) ++nf;
+      }
+      nan = ln != NO_ID;
+    } else {
+#pragma unroll
+      for (int k = 0; k < EPT; ++k) {
+        lm = fmaxf(lm, x[k]);
+        nan |= x[k] != x[k];
       }
     }
+    float wm = lm;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const float om = __shfl_xor_sync(0xffffffffu, lm, o);
-      const int32_t oa = __shfl_xor_sync(0xffffffffu, la, o);
-      if (om > lm || (om == lm && oa < la)) {
-        lm = om;
+      const float om = __shfl_xor_sync(FULL, wm, o);
+      const int32_t oa = __shfl_xor_sync(FULL, la, o);
+      if (om > wm || (om == wm && oa < la)) {
+        wm = om;
         la = oa;
       }
-      ln = min(ln, __shfl_xor_sync(0xffffffffu, ln, o));
-      nf += __shfl_xor_sync(0xffffffffu, nf, o);
-      pinf |= __shfl_xor_sync(0xffffffffu, pinf, o);
+      ln = min(ln, __shfl_xor_sync(FULL, ln, o));
     }
+    const bool wnan = __any_sync(FULL, nan);
     if (lane == 0) {
-      sm.wf[warp] = lm;
+      sm.wf[warp] = wm;
       sm.wi[warp] = la;
       sm.wi2[warp] = ln;
-      sm.wu[warp] = nf;
-      sm.wu2[warp] = pinf;
+      sm.wu2[warp] = wnan;
     }
     __syncthreads();
     if (tid == 0) {
       float m = NEG;
       int32_t am = NO_ID, an = NO_ID;
-      uint32_t n = 0, p = 0;
+      uint32_t p = 0;
       for (int w = 0; w < NW; ++w) {
         if (sm.wf[w] > m || (sm.wf[w] == m && sm.wi[w] < am)) {
           m = sm.wf[w];
           am = sm.wi[w];
         }
         an = min(an, sm.wi2[w]);
-        n += sm.wu[w];
         p |= sm.wu2[w];
       }
       sm.stat.mx = m;
       sm.stat.amax = am;
-      sm.stat.nan_id = an;
-      sm.stat.nfin = n;
-      sm.stat.pinf = p;
-      sm.stat.status = sm.status;
+      sm.stat.nan = p;
+      sm.stat.status = sm.status | sm.status_g | sm.status_u;
+      sm.red_i[1] = an;
     }
     Clu<CS>::sync();
     gmax = NEG;
-    gamax = NO_ID;
-    gnan = NO_ID;
-    gnfin = 0;
-    gpinf = false;
     gstatus = 0;
+    uint32_t gn = 0;
 #pragma unroll
     for (int r = 0; r < CS; ++r) {
       const StatX s = *Clu<CS>::at(&sm.stat, r);
@@ -719,37 +943,94 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         gmax = s.mx;
         gamax = s.amax;
       }
-      gnan = min(gnan, s.nan_id);
-      gnfin += s.nfin;
-      gpinf |= s.pinf != 0;
+      gn |= s.nan;
       gstatus |= s.status;
+      if (sel == MTR_SELECT_ARGMAX) gnan = min(gnan, *Clu<CS>::at(&sm.red_i[1], r));
     }
+    if (gn && gnan == NO_ID) gnan = NO_ID - 1;  // NaN present (its id only matters for argmax)
   }
-  const bool nonfinite = gnan != NO_ID || gpinf;
+  const bool nonfinite = gnan != NO_ID || gmax == pos_inf();
   const bool all_masked = !nonfinite && gmax == NEG;
   if (nonfinite) gstatus |= MTR_ROW_NONFINITE;
   if (all_masked) gstatus |= MTR_ROW_ALL_MASKED;
   const bool clean = !nonfinite && !all_masked;
-  const int sel = a.select_mode;
-  const bool force_radix = (a.flags & MTR_FLAG_FORCE_RADIX) != 0;
 
   // selection state
-  float tk = NEG;           // top-k threshold (keep x >= tk)
+  float tk = NEG;           // top-k threshold: survivors are finite x >= tk
+  bool topk_active = false;
+  uint32_t nsurv = 0;       // survivors (valid when topk_active)
+  bool list_ready = false;  // the candidate list holds every survivor
+  int list_n = 0;
   bool topp_cut = false;    // keep also requires canonical <= (cut_x, cut_id)
   float cut_x = 0.0f;
   int32_t cut_id = NO_ID;
   u64 qkept = 0;
   int32_t token = -1;
   int owner = 0;            // cluster rank that writes the row's scalar outputs
-  uint32_t q[EPT];
-#pragma unroll
-  for (int k = 0; k < EPT; ++k) q[k] = 0u;
+  const float* lx = sm.cx;
+  const int32_t* lid = sm.cid;
+  uint32_t* lq = sm.cq;
   const bool want_lp = a.out_logprobs != nullptr;
   const bool need_mass = clean && (sel == MTR_SELECT_SAMPLE || want_lp || (sel == MTR_SELECT_NONE && dv.topp_on));
+  uint32_t qz[EPT];  // placeholder when collecting without probabilities
+#pragma unroll
+  for (int k = 0; k < EPT; ++k) qz[k] = 0u;
 
-  // radix fallback: finds v with W(> v) <= lim < W(>= v) among candidates
-  // (pred), descending by key, weights wt; above0 = weight ranked above all
-  // candidates.  Returns v, W(> v) and the count / weight of key == v.
+  // finite-element count of the row (block + cluster)
+  auto count_finite = [&]() -> uint32_t {
+    uint32_t nf = 0;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) nf += finite_val(x[k]);
+    nf = warp_sum_u32(nf);
+    Clu<CS>::sync();  // wu / cta_nfin free for reuse
+    if (lane == 0) sm.wu[warp] = nf;
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t t = 0;
+      for (int w = 0; w < NW; ++w) t += sm.wu[w];
+      sm.cta_nfin = t;
+    }
+    Clu<CS>::sync();
+    uint32_t t = 0;
+#pragma unroll
+    for (int r = 0; r < CS; ++r) t += *Clu<CS>::at(&sm.cta_nfin, r);
+    return t;
+  };
+
+  // merged histogram counts / masses (CS > 1 sums every CTA's bins)
+  auto merged_counts = [&](int nbins) -> const uint32_t* {
+    if constexpr (CS == 1) {
+      return sm.hcnt;
+    } else {
+      for (int i = tid; i < nbins; i += THREADS) {
+        uint32_t c = 0;
+#pragma unroll
+        for (int r = 0; r < CS; ++r) c += Clu<CS>::at(sm.hcnt, r)[i];
+        sm.hcnt_m[i] = c;
+      }
+      __syncthreads();
+      return sm.hcnt_m;
+    }
+  };
+  auto merged_masses = [&](int nbins) -> const u64* {
+    if constexpr (CS == 1) {
+      return sm.hmass;
+    } else {
+      for (int i = tid; i < nbins; i += THREADS) {
+        u64 m = 0;
+#pragma unroll
+        for (int r = 0; r < CS; ++r) m += Clu<CS>::at(sm.hmass, r)[i];
+        sm.hmass_m[i] = m;
+      }
+      __syncthreads();
+      return sm.hmass_m;
+    }
+  };
+
+  // radix fallback over this CTA's elements: finds v with W(> v) <= lim <
+  // W(>= v) among candidates (pred), descending by key, weights wt; above0 =
+  // weight ranked above all candidates.  Returns v, W(> v) and the count /
+  // weight of key == v.
   auto radix_select = [&](auto pred, auto keyf, auto wt, u64 lim, u64 above0, uint32_t& out_key, u64& out_above,
                           uint32_t& out_cnt, u64& out_w) {
     uint32_t prefix = 0, mask = 0;
@@ -759,7 +1040,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
 #pragma unroll 1
     for (int shift = 24; shift >= 0; shift -= 8) {
       Clu<CS>::sync();  // previous readers of the histograms are done
-      for (int i = tid; i < NB; i += THREADS) {
+      for (int i = tid; i < 256; i += THREADS) {
         sm.hcnt[i] = 0u;
         sm.hmass[i] = 0ull;
       }
@@ -776,25 +1057,9 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         }
       }
       Clu<CS>::sync();
-      const uint32_t* hc = sm.hcnt;
-      const u64* hm = sm.hmass;
-      if constexpr (CS > 1) {
-        for (int i = tid; i < NB; i += THREADS) {
-          uint32_t c = 0;
-          u64 m = 0;
-#pragma unroll
-          for (int r = 0; r < CS; ++r) {
-            c += Clu<CS>::at(sm.hcnt, r)[i];
-            m += Clu<CS>::at(sm.hmass, r)[i];
-          }
-          sm.hcnt_m[i] = c;
-          sm.hmass_m[i] = m;
-        }
-        __syncthreads();
-        hc = sm.hcnt_m;
-        hm = sm.hmass_m;
-      }
-      find_crossing(hm, lim - above, &sm.cr);
+      const uint32_t* hc = merged_counts(256);
+      const u64* hm = merged_masses(256);
+      find_crossing<256>(hm, lim - above, &sm.cr);
       const int b = max(sm.cr.bin, 0);  // a crossing exists: above <= lim < above + candidates
       const uint32_t d = 255u - (uint32_t)b;
       prefix |= d << shift;
@@ -810,14 +1075,16 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     out_w = lastw;
   };
 
-  // merge the per-CTA candidate lists into (mcx, mcid, mcq); returns the total
-  auto merge_lists = [&](int& n_total, const float*& lx, const int32_t*& lid, const uint32_t*& lq) {
+  // merge the per-CTA candidate lists; returns the total (entries stored only
+  // when the total fits CAP).  After it every CTA of the cluster holds the
+  // same merged list, so list-only stages need no further exchange.
+  auto merge_lists = [&]() -> int {
     Clu<CS>::sync();
     if constexpr (CS == 1) {
-      n_total = sm.nc;
       lx = sm.cx;
       lid = sm.cid;
       lq = sm.cq;
+      return sm.nc;
     } else {
       int tot = 0;
       int offs[CS];
@@ -826,7 +1093,6 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         offs[r] = tot;
         tot += *Clu<CS>::at(&sm.nc, r);
       }
-      n_total = tot;
       if (tot <= CAP) {
 #pragma unroll
         for (int r = 0; r < CS; ++r) {
@@ -845,213 +1111,312 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       lx = sm.mcx;
       lid = sm.mcid;
       lq = sm.mcq;
+      return tot;
     }
+  };
+
+  // start a new local candidate list (after every reader of the previous one)
+  auto reset_list = [&]() {
+    Clu<CS>::sync();
+    if (tid == 0) sm.nc = 0;
+    __syncthreads();
+  };
+
+  // exact k-th value among n listed values: thread i counts the entries above it
+  auto kth_in_list = [&](int n, u64 above, u64 lim) {
+    if (tid < n) {
+      const float xi = lx[tid];
+      uint32_t gt = 0, ge = 0;
+      for (int jj = 0; jj < n; ++jj) {
+        const float xj = lx[jj];
+        gt += xj > xi;
+        ge += xj >= xi;
+      }
+      if (above + gt <= lim && lim < above + ge) {
+        sm.tk = xi;
+        sm.nsurv = (uint32_t)(above + ge);
+      }
+    }
+    __syncthreads();
+  };
+
+  // zero the 1024-entry mass histogram (CTA-local use only)
+  auto zero_hmass = [&]() {
+    for (int i = tid * 2; i < NB; i += THREADS * 2) *(uint4*)(sm.hmass + i) = make_uint4(0u, 0u, 0u, 0u);
+  };
+
+  // entries of the list (index < n) that satisfy `pred` move to the crossing-bin
+  // list; returns its size (entries past MINI are counted only)
+  auto gather_mini = [&](int n, auto pred) -> int {
+    if (tid == 0) sm.nm = 0;
+    __syncthreads();
+    if (tid < n && pred(tid)) {
+      const int s = atomicAdd(&sm.nm, 1);
+      if (s < MINI) {
+        sm.nx[s] = lx[tid];
+        sm.nid[s] = lid[tid];
+        sm.nq[s] = lq[tid];
+      }
+    }
+    __syncthreads();
+    return sm.nm;
   };
 
   // ------------------------------------------------------------ selection
   if (clean && sel == MTR_SELECT_ARGMAX) {
     token = gamax;
-  } else if (clean && sel != MTR_SELECT_ARGMAX) {
+  } else if (clean) {
     // ---------------- top-k
-    uint32_t nsurv = gnfin;
-    const bool topk_on = dv.topk_on && (uint32_t)a.top_k < gnfin;
-    if (topk_on) {
+    if (dv.topk_on) {
       const u64 lim = (u64)(a.top_k - 1);
-      for (int i = tid; i < NB; i += THREADS) sm.hcnt[i] = 0u;
-      if (tid == 0) sm.nc = 0;
-      __syncthreads();
+      bool done = false;
+      if (!force_radix) {
+        // bound from the per-thread maxima: every thread whose maximum lies in
+        // bins <= btau owns at least one element there, so >= k elements do
+        if (lm > NEG) atomicAdd(&sm.hcnt[dbin(gmax, lm)], 1u);
+        Clu<CS>::sync();
+        find_crossing<NB>(merged_counts(NB), lim, &sm.cr);
+        const int btau = sm.cr.bin;
+        if (btau >= 0) {
+          const float c = btau >= NB - 1 ? pos_inf() : (float)(btau + 1) * (1.0f / BIN_SCALE);
+          uint32_t mask = 0;
 #pragma unroll
-      for (int k = 0; k < EPT; ++k)
-        if (finite_val(x[k])) atomicAdd(&sm.hcnt[dbin(gmax, x[k])], 1u);
-      Clu<CS>::sync();
-      const uint32_t* hc = sm.hcnt;
-      if constexpr (CS > 1) {
-        for (int i = tid; i < NB; i += THREADS) {
-          uint32_t c = 0;
-#pragma unroll
-          for (int r = 0; r < CS; ++r) c += Clu<CS>::at(sm.hcnt, r)[i];
-          sm.hcnt_m[i] = c;
-        }
-        __syncthreads();
-        hc = sm.hcnt_m;
-      }
-      find_crossing(hc, lim, &sm.cr);
-      const int bstar = max(sm.cr.bin, 0);  // k - 1 < finite count, so a crossing exists
-      const u64 c_above = sm.cr.above;
-      const u64 n_c = sm.cr.w;
-      if (n_c <= (u64)CAP && !force_radix) {
-#pragma unroll
-        for (int k = 0; k < EPT; ++k)
-          if (finite_val(x[k]) && dbin(gmax, x[k]) == bstar) sm.cx[atomicAdd(&sm.nc, 1)] = x[k];
-        int n;
-        const float* lx;
-        const int32_t* lid;
-        const uint32_t* lq;
-        merge_lists(n, lx, lid, lq);
-        if (tid < n) {
-          const float xi = lx[tid];
-          uint32_t gt = 0, ge = 0;
-          for (int jj = 0; jj < n; ++jj) {
-            const float xj = lx[jj];
-            gt += xj > xi;
-            ge += xj >= xi;
+          for (int k = 0; k < EPT; ++k) mask |= (uint32_t)(__fsub_rn(gmax, x[k]) < c) << k;
+          collect<CS, EPT>(sm, mask, x, qz, false, id_of, lane);
+          const int n = merge_lists();
+          if (n <= CAP) {
+            // second level: count histogram over the listed values
+            for (int i = tid; i < NB; i += THREADS) sm.hcnt[i] = 0u;
+            __syncthreads();
+            if (tid < n) atomicAdd(&sm.hcnt[dbin(gmax, lx[tid])], 1u);
+            __syncthreads();
+            find_crossing<NB>(sm.hcnt, lim, &sm.cr);
+            const int b2 = max(sm.cr.bin, 0);  // n >= k, so a crossing exists
+            const u64 above2 = sm.cr.above;
+            const int m = gather_mini(n, [&](int i) { return dbin(gmax, lx[i]) == b2; });
+            if (m <= MINI) {
+              if (tid < m) {
+                const float xi = sm.nx[tid];
+                uint32_t gt = 0, ge = 0;
+                for (int jj = 0; jj < m; ++jj) {
+                  const float xj = sm.nx[jj];
+                  gt += xj > xi;
+                  ge += xj >= xi;
+                }
+                if (above2 + gt <= lim && lim < above2 + ge) {
+                  sm.tk = xi;
+                  sm.nsurv = (uint32_t)(above2 + ge);
+                }
+              }
+              __syncthreads();
+            } else {
+              kth_in_list(n, 0ull, lim);
+            }
+            tk = sm.tk;
+            nsurv = sm.nsurv;
+            topk_active = true;
+            list_ready = true;
+            list_n = n;
+            done = true;
           }
-          if (c_above + gt <= lim && lim < c_above + ge) {
-            sm.tk = xi;
-            sm.nsurv = (uint32_t)(c_above + ge);
-          }
         }
-        __syncthreads();
-        tk = sm.tk;
-        nsurv = sm.nsurv;
-      } else {
-        uint32_t key, cntv;
-        u64 abv, wv;
-        radix_select([&](int k) { return finite_val(x[k]) && dbin(gmax, x[k]) == bstar; },
-                     [&](int k) { return fkey(x[k]); }, [&](int) { return 1u; }, lim, c_above, key, abv, cntv, wv);
-        tk = key2f(key);
-        nsurv = (uint32_t)(abv + wv);
-        gstatus |= MTR_ROW_SLOW_PATH;
       }
+      if (!done) {
+        const uint32_t nfin = count_finite();
+        if ((u64)a.top_k < (u64)nfin) {
+          topk_active = true;
+          Clu<CS>::sync();
+          for (int i = tid; i < NB; i += THREADS) sm.hcnt[i] = 0u;
+          __syncthreads();
 #pragma unroll
-      for (int k = 0; k < EPT; ++k)
-        if (x[k] < tk) x[k] = NEG;
+          for (int k = 0; k < EPT; ++k)
+            if (finite_val(x[k])) atomicAdd(&sm.hcnt[dbin(gmax, x[k])], 1u);
+          Clu<CS>::sync();
+          find_crossing<NB>(merged_counts(NB), lim, &sm.cr);
+          const int bstar = max(sm.cr.bin, 0);  // k - 1 < finite count, so a crossing exists
+          const u64 c_above = sm.cr.above;
+          const u64 n_c = sm.cr.w;
+          if (n_c <= (u64)CAP && !force_radix) {
+            reset_list();
+            uint32_t mask = 0;
+#pragma unroll
+            for (int k = 0; k < EPT; ++k) mask |= (uint32_t)(finite_val(x[k]) && dbin(gmax, x[k]) == bstar) << k;
+            collect<CS, EPT>(sm, mask, x, qz, false, id_of, lane);
+            const int n = merge_lists();
+            kth_in_list(n, c_above, lim);
+            tk = sm.tk;
+            nsurv = sm.nsurv;
+          } else {
+            uint32_t key, cntv;
+            u64 abv, wv;
+            radix_select([&](int k) { return finite_val(x[k]) && dbin(gmax, x[k]) == bstar; },
+                         [&](int k) { return fkey(x[k]); }, [&](int) { return 1u; }, lim, c_above, key, abv, cntv,
+                         wv);
+            tk = key2f(key);
+            nsurv = (uint32_t)(abv + wv);
+            gstatus |= MTR_ROW_SLOW_PATH;
+          }
+        } else {
+          nsurv = nfin;  // fewer than k finite scores: top-k removes nothing
+        }
+      }
     }
 
     // ---------------- top-p and the draw
     if (need_mass) {
       const bool topp_on = dv.topp_on != 0;
       const float u = sm.u;
-      if (nsurv <= (uint32_t)CAP && !force_radix) {
-        // compact path: every survivor in one list
-        Clu<CS>::sync();
-        if (tid == 0) sm.nc = 0;
-        __syncthreads();
+      if (topk_active && nsurv <= (uint32_t)CAP && !force_radix) {
+        // compact path: every survivor is in the list; other entries get q = 0
+        if (!list_ready) {
+          reset_list();
+          uint32_t mask = 0;
 #pragma unroll
-        for (int k = 0; k < EPT; ++k) {
-          if (finite_val(x[k])) {
-            const int s = atomicAdd(&sm.nc, 1);
-            sm.cx[s] = x[k];
-            sm.cid[s] = id_of(k);
-            sm.cq[s] = expfx(__fsub_rn(x[k], gmax));
-          }
+          for (int k = 0; k < EPT; ++k) mask |= (uint32_t)(finite_val(x[k]) && x[k] >= tk) << k;
+          collect<CS, EPT>(sm, mask, x, qz, false, id_of, lane);
+          list_n = merge_lists();
         }
-        int n;
-        const float* lx;
-        const int32_t* lid;
-        const uint32_t* lq;
-        merge_lists(n, lx, lid, lq);
+        const int n = list_n;
         float xi = 0.0f;
         int32_t ii = 0;
-        u64 qi = 0, ai = 0, tot = 0;
+        uint32_t qi = 0;
         if (tid < n) {
           xi = lx[tid];
           ii = lid[tid];
-          qi = lq[tid];
-          for (int jj = 0; jj < n; ++jj) {
-            const float xj = lx[jj];
-            const u64 qj = lq[jj];
-            tot += qj;
-            if (xj > xi || (xj == xi && lid[jj] < ii)) ai += qj;
-          }
-          if (tid == 0) sm.qtot = tot;
+          qi = xi >= tk ? expfx(__fsub_rn(xi, gmax)) : 0u;
+          lq[tid] = qi;
         }
-        __syncthreads();
-        tot = sm.qtot;
-        bool kept = tid < n;
+        // total mass
+        {
+          const u64 s = warp_sum_u64((u64)qi);
+          if (lane == 0) sm.wl[warp] = s;
+          zero_hmass();
+          __syncthreads();
+          u64 t = 0;
+#pragma unroll
+          for (int w = 0; w < NW; ++w) t += sm.wl[w];
+          qkept = t;
+        }
+        const u64 tot = qkept;
         if (topp_on) {
           const double P = __dmul_rn((double)a.top_p, (double)tot);
           const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
-          kept = kept && ai <= plim;
-          if (kept && ai + qi > plim) {
-            sm.cut_x = xi;
-            sm.cut_id = ii;
-            sm.qkept = ai + qi;
+          if (qi) atomicAdd(&sm.hmass[dbin(gmax, xi)], (u64)qi);
+          __syncthreads();
+          find_crossing<NB>(sm.hmass, plim, &sm.cr);
+          const int b3 = max(sm.cr.bin, 0);  // plim < total
+          const u64 above3 = sm.cr.above;
+          const int m = gather_mini(n, [&](int i) { return lq[i] != 0u && dbin(gmax, lx[i]) == b3; });
+          if (m <= MINI) {
+            if (tid < m) {
+              const float xm = sm.nx[tid];
+              const int32_t im = sm.nid[tid];
+              const u64 qm = sm.nq[tid];
+              u64 am = above3;
+              for (int jj = 0; jj < m; ++jj)
+                if (canon_before(sm.nx[jj], sm.nid[jj], xm, im)) am += sm.nq[jj];
+              if (am <= plim && am + qm > plim) {
+                sm.cut_x = xm;
+                sm.cut_id = im;
+                sm.qkept = am + qm;
+              }
+            }
+          } else if (tid < n && qi) {
+            u64 ai = 0;
+            for (int jj = 0; jj < n; ++jj)
+              if (canon_before(lx[jj], lid[jj], xi, ii)) ai += lq[jj];
+            if (ai <= plim && ai + qi > plim) {
+              sm.cut_x = xi;
+              sm.cut_id = ii;
+              sm.qkept = ai + qi;
+            }
           }
-        } else if (tid == 0) {
-          sm.qkept = tot;
-        }
-        if (tid < CAP) sm.ckeep[tid] = kept ? 1 : 0;
-        __syncthreads();
-        qkept = sm.qkept;
-        if (topp_on) {
+          __syncthreads();
           topp_cut = true;
           cut_x = sm.cut_x;
           cut_id = sm.cut_id;
-          if (tid < n && xi == cut_x && ii > cut_id) atomicOr(&sm.status, MTR_ROW_TIE_AT_CUT);
+          qkept = sm.qkept;
+        }
+        const bool kept = qi != 0u && (!topp_cut || xi > cut_x || (xi == cut_x && ii <= cut_id));
+        if (topp_cut) {
+          const bool tie = tid < n && xi >= tk && xi == cut_x && ii > cut_id;
+          if (__syncthreads_or(tie)) gstatus |= MTR_ROW_TIE_AT_CUT;
         }
         if (sel == MTR_SELECT_SAMPLE) {
+          // id-binned kept mass, then the exact draw inside the crossing id bin
           const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
-          if (kept) {
+          zero_hmass();
+          if (tid < CAP) sm.ckeep[tid] = kept ? 1 : 0;
+          __syncthreads();
+          if (kept) atomicAdd(&sm.hmass[ii >> dv.id_shift], (u64)qi);
+          __syncthreads();
+          find_crossing<NB>(sm.hmass, R, &sm.cr);
+          const int b4 = max(sm.cr.bin, 0);  // R < qkept
+          const u64 above4 = sm.cr.above;
+          const int m = gather_mini(n, [&](int i) { return sm.ckeep[i] && (lid[i] >> dv.id_shift) == b4; });
+          if (m <= MINI) {
+            if (tid < m) {
+              const int32_t im = sm.nid[tid];
+              const u64 qm = sm.nq[tid];
+              u64 cm = above4;
+              for (int jj = 0; jj < m; ++jj)
+                if (sm.nid[jj] <= im) cm += sm.nq[jj];
+              if (cm > R && cm - qm <= R) sm.token = im;
+            }
+          } else if (kept) {
             u64 ci = 0;
             for (int jj = 0; jj < n; ++jj)
               if (sm.ckeep[jj] && lid[jj] <= ii) ci += lq[jj];
             if (ci > R && ci - qi <= R) sm.token = ii;
           }
+          __syncthreads();
+          token = sm.token;
         }
-        __syncthreads();
-        gstatus |= sm.status & MTR_ROW_TIE_AT_CUT;
-        token = sm.token;
       } else {
-        // dense path: per-element fixed-point probabilities
+        // dense path: per-element fixed-point probabilities of the survivors
+        uint32_t q[EPT];
 #pragma unroll
-        for (int k = 0; k < EPT; ++k) q[k] = finite_val(x[k]) ? expfx(__fsub_rn(x[k], gmax)) : 0u;
+        for (int k = 0; k < EPT; k += 2) {
+          expfx2(__fsub_rn(x[k], gmax), __fsub_rn(x[k + 1], gmax), q[k], q[k + 1]);
+          if (!(x[k] >= tk)) q[k] = 0u;
+          if (!(x[k + 1] >= tk)) q[k + 1] = 0u;
+        }
         if (topp_on) {
           Clu<CS>::sync();
-          for (int i = tid; i < NB; i += THREADS) sm.hmass[i] = 0ull;
+          zero_hmass();
           if (tid == 0) sm.nc = 0;
           __syncthreads();
 #pragma unroll
           for (int k = 0; k < EPT; ++k)
             if (q[k]) atomicAdd(&sm.hmass[dbin(gmax, x[k])], (u64)q[k]);
           Clu<CS>::sync();
-          const u64* hm = sm.hmass;
-          if constexpr (CS > 1) {
-            for (int i = tid; i < NB; i += THREADS) {
-              u64 m = 0;
-#pragma unroll
-              for (int r = 0; r < CS; ++r) m += Clu<CS>::at(sm.hmass, r)[i];
-              sm.hmass_m[i] = m;
-            }
-            __syncthreads();
-            hm = sm.hmass_m;
-          }
+          const u64* hm = merged_masses(NB);
           // total first, then the crossing of plim
-          find_crossing(hm, ~0ull - 1ull, &sm.cr);
+          find_crossing<NB>(hm, ~0ull - 1ull, &sm.cr);
           const u64 tot = sm.cr.total;
           const double P = __dmul_rn((double)a.top_p, (double)tot);
           const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
           __syncthreads();
-          find_crossing(hm, plim, &sm.cr);
+          find_crossing<NB>(hm, plim, &sm.cr);
           const int bstar = max(sm.cr.bin, 0);  // plim < total since top_p < 1
           const u64 w_above = sm.cr.above;
+          const float lo = (float)bstar * (1.0f / BIN_SCALE), hi = (float)(bstar + 1) * (1.0f / BIN_SCALE);
+          uint32_t mask = 0;
 #pragma unroll
           for (int k = 0; k < EPT; ++k) {
-            if (q[k] && dbin(gmax, x[k]) == bstar) {
-              const int s = atomicAdd(&sm.nc, 1);
-              if (s < CAP) {
-                sm.cx[s] = x[k];
-                sm.cid[s] = id_of(k);
-                sm.cq[s] = q[k];
-              }
-            }
+            const float d = __fsub_rn(gmax, x[k]);
+            mask |= (uint32_t)(q[k] != 0u && d >= lo && (bstar >= NB - 1 || d < hi)) << k;
           }
-          int n;
-          const float* lx;
-          const int32_t* lid;
-          const uint32_t* lq;
-          // per-CTA overflow is detected through the merged total
-          merge_lists(n, lx, lid, lq);
+          collect<CS, EPT>(sm, mask, x, q, true, id_of, lane);
+          const int n = merge_lists();
           if (n <= CAP && !force_radix) {
             if (tid < n) {
               const float xi = lx[tid];
               const int32_t ii = lid[tid];
               const u64 qi = lq[tid];
               u64 ai = w_above;
-              for (int jj = 0; jj < n; ++jj) {
-                const float xj = lx[jj];
-                if (xj > xi || (xj == xi && lid[jj] < ii)) ai += lq[jj];
-              }
+              for (int jj = 0; jj < n; ++jj)
+                if (canon_before(lx[jj], lid[jj], xi, ii)) ai += lq[jj];
               if (ai <= plim && ai + qi > plim) {
                 sm.cut_x = xi;
                 sm.cut_id = ii;
@@ -1062,9 +1427,8 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
             cut_x = sm.cut_x;
             cut_id = sm.cut_id;
             qkept = sm.qkept;
-            if (tid < n && lx[tid] == cut_x && lid[tid] > cut_id) atomicOr(&sm.status, MTR_ROW_TIE_AT_CUT);
-            __syncthreads();
-            gstatus |= sm.status & MTR_ROW_TIE_AT_CUT;
+            const bool tie = tid < n && lx[tid] == cut_x && lid[tid] > cut_id;
+            if (__syncthreads_or(tie)) gstatus |= MTR_ROW_TIE_AT_CUT;
           } else {
             uint32_t key, cntv;
             u64 abv, wv;
@@ -1096,6 +1460,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
 #pragma unroll
           for (int k = 0; k < EPT; ++k) s += q[k];
           s = warp_sum_u64(s);
+          Clu<CS>::sync();
           if (lane == 0) sm.wl[warp] = s;
           __syncthreads();
           if (tid == 0) {
@@ -1114,8 +1479,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
 #pragma unroll
           for (int k = 0; k < EPT; ++k) {
             const float v = x[k];
-            const bool kp = v > cut_x || (v == cut_x && id_of(k) <= cut_id);
-            if (!kp) q[k] = 0u;
+            if (!(v > cut_x || (v == cut_x && id_of(k) <= cut_id))) q[k] = 0u;
           }
         }
         if (sel == MTR_SELECT_SAMPLE) {
@@ -1184,17 +1548,17 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
             const u64 excl = wbefore + incl - mine;
             if (mine != 0 && excl <= rr && rr < excl + mine) {
               u64 c = excl;
-              bool done = false;
+              bool found = false;
 #pragma unroll
               for (int j = 0; j < NCH; ++j) {
 #pragma unroll
                 for (int e = 0; e < VEC; ++e) {
                   const int k = j * VEC + e;
-                  if (j == jstar && !done) {
+                  if (j == jstar && !found) {
                     c += q[k];
                     if (c > rr) {
                       sm.token = id_of(k);
-                      done = true;
+                      found = true;
                     }
                   }
                 }
@@ -1213,18 +1577,20 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   // ------------------------------------------------------------ epilogue
   // processed scores: survivors of top-k and top-p; unfiltered for argmax
   const bool filter_out = clean && sel != MTR_SELECT_ARGMAX;
+  auto kept_at = [&](float v, int id) -> bool {
+    if (!(v >= tk)) return false;
+    return !topp_cut || v > cut_x || (v == cut_x && id <= cut_id);
+  };
   if (a.out_scores) {
     float* orow = a.out_scores + row * a.out_scores_row_stride;
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
-      const int id0 = base + (j * THREADS + tid) * VEC;
+      const int id0 = chunk_id(j);
       float o[VEC];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
-        const int k = j * VEC + e;
-        float v = x[k];
-        if (filter_out && topp_cut && !(v > cut_x || (v == cut_x && id0 + e <= cut_id))) v = NEG;
-        o[e] = v;
+        const float v = x[j * VEC + e];
+        o[e] = (filter_out && !kept_at(v, id0 + e)) ? NEG : v;
       }
       if (dv.out_vec && id0 < V) {
 #pragma unroll
@@ -1264,14 +1630,13 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     }
 #pragma unroll
     for (int j = 0; j < NCH; ++j) {
-      const int id0 = base + (j * THREADS + tid) * VEC;
+      const int id0 = chunk_id(j);
       float o[VEC];
 #pragma unroll
       for (int e = 0; e < VEC; ++e) {
-        const int k = j * VEC + e;
-        const float v = x[k];
+        const float v = x[j * VEC + e];
         bool kp = finite_val(v);
-        if (filter_out && topp_cut) kp = kp && (v > cut_x || (v == cut_x && id0 + e <= cut_id));
+        if (filter_out) kp = kp && kept_at(v, id0 + e);
         o[e] = !clean ? __int_as_float(0x7fc00000) : kp ? (float)(((double)v - (double)gmax) - lse) : NEG;
       }
       if (dv.lp_vec && id0 < V) {
@@ -1312,8 +1677,13 @@ struct Geo {
   int threads, ept, cs;
 };
 
-static Geo pick_geo(int V) {
-  if (V <= 4096) return {256, 16, 1};
+// Few rows of a small vocabulary: split each row over a cluster pair so more
+// SMs work on the step (latency); otherwise one CTA (or cluster) per row.
+static Geo pick_geo(int V, int64_t B, int sms) {
+  if (V <= 4096) {
+    if (B * 2 <= sms) return {256, 8, 2};
+    return {256, 16, 1};
+  }
   if (V <= 8192) return {256, 16, 2};
   if (V <= 16384) return {256, 16, 4};
   if (V <= 32768) return {512, 16, 4};
@@ -1325,6 +1695,26 @@ static int dyn_smem_bytes(const Geo& g, bool pen) {
   if (!pen) return 0;
   const int tile = g.threads * g.ept;
   return tile * 4 + tile * 4 + tile * 2;
+}
+
+// SM count of the current device (148 when no device is visible, e.g. for
+// geometry queries on a CPU-only host)
+static int device_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cache[dev] = n;
+  }
+  return cache[dev];
 }
 
 static thread_local int g_last_cuda_error = 0;
@@ -1376,7 +1766,7 @@ static int validate(const MtrSamplerArgs* a) {
     if (!a->grammar_allow) return MTR_ERR_NULL_ARG;
     if (a->grammar_n_classes < 1 || a->grammar_n_classes > MTR_MAX_GRAMMAR_CLASSES) return MTR_ERR_BAD_PARAM;
     if (!(a->flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) && !a->prev_token) return MTR_ERR_NULL_ARG;
-    if ((uintptr_t)a->grammar_allow % 4) return MTR_ERR_ALIGNMENT;
+    if ((uintptr_t)a->grammar_allow % 4 || (uintptr_t)a->grammar_vocab_bits % 4) return MTR_ERR_ALIGNMENT;
   }
   if ((uintptr_t)a->prev_token % 4) return MTR_ERR_ALIGNMENT;
   // penalties
@@ -1440,6 +1830,9 @@ static Derived derive(const MtrSamplerArgs& a) {
   d.topk_on = a.select_mode != MTR_SELECT_ARGMAX && a.top_k > 0 && a.top_k < a.vocab;
   d.topp_on = a.select_mode != MTR_SELECT_ARGMAX && a.top_p < 1.0f;
   d.ids_len = a.input_ids ? a.ids_len : 0;
+  d.id_shift = 0;
+  while (((a.vocab - 1) >> d.id_shift) >= NB) ++d.id_shift;
+  d.gwords = (a.vocab + 31) / 32;
   d.temp_rcp = 1.0f / a.temperature;
   for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c)
     d.cond_rcp[c] = (c < a.n_cond && a.cond_temperature[c] > 0.0f) ? 1.0f / a.cond_temperature[c] : 1.0f;
@@ -1458,7 +1851,7 @@ static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, 
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::call_once(once[dev], [&]() {
-    const int max_dyn = 227 * 1024 - (int)sizeof(Shared<CS, EPT / Elem<Tin>::VEC>);
+    const int max_dyn = 227 * 1024 - (int)sizeof(Shared<CS>);
     attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn);
   });
   if (attr_err[dev] != cudaSuccess) return attr_err[dev];
@@ -1482,6 +1875,7 @@ static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, 
 
 template <typename Tin>
 static cudaError_t launch_dtype(const MtrSamplerArgs& a, const Derived& d, const Geo& g, int dyn, cudaStream_t s) {
+  if (g.threads == 256 && g.ept == 8 && g.cs == 2) return launch_t<Tin, 256, 8, 2>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 1) return launch_t<Tin, 256, 16, 1>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 2) return launch_t<Tin, 256, 16, 2>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 4) return launch_t<Tin, 256, 16, 4>(a, d, dyn, s);
@@ -1521,7 +1915,7 @@ int mtr_sampler_validate(const MtrSamplerArgs* a) { return mtr::validate(a); }
 int mtr_sampler_query(int32_t vocab, int32_t num_rows, int32_t with_penalties, MtrLaunchInfo* out) {
   if (!out) return MTR_ERR_NULL_ARG;
   if (vocab < 1 || vocab > MTR_MAX_VOCAB || num_rows < 0) return MTR_ERR_BAD_SHAPE;
-  const mtr::Geo g = mtr::pick_geo(vocab);
+  const mtr::Geo g = mtr::pick_geo(vocab, num_rows, mtr::device_sms());
   out->threads = g.threads;
   out->elems_per_thread = g.ept;
   out->cluster_size = g.cs;
@@ -1538,7 +1932,7 @@ int mtr_sampler_launch(const MtrSamplerArgs* a, void* stream) {
   if (v != MTR_OK) return v;
   if (a->num_rows == 0) return MTR_OK;
   const mtr::Derived d = mtr::derive(*a);
-  const mtr::Geo g = mtr::pick_geo(a->vocab);
+  const mtr::Geo g = mtr::pick_geo(a->vocab, a->num_rows, mtr::device_sms());
   const int dyn = mtr::dyn_smem_bytes(g, d.pen_on != 0);
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;

@@ -229,6 +229,7 @@ class FusedLogitsProcessor(_LogitsProcessorBase):
         if self.grammar is not None:
             a.grammar_class_of = self.grammar.class_of.data_ptr()
             a.grammar_allow = self.grammar.allow.data_ptr()
+            a.grammar_vocab_bits = self.grammar.bits().data_ptr()
             a.grammar_n_classes = self.grammar.allow.numel()
             a.flags |= N.FLAG_GRAMMAR_PREV_FROM_IDS
         a.repetition_penalty = self.repetition_penalty

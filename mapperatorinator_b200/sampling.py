@@ -122,6 +122,25 @@ class GrammarTable:
 
     class_of: torch.Tensor  # [V] uint8
     allow: torch.Tensor     # [C] int32 (bit patterns)
+    vocab_bits: torch.Tensor | None = None  # [C, ceil(V/32)] int32, built on first use
+
+    def bits(self) -> torch.Tensor:
+        """Per-class vocabulary bitmaps (bit v of row c = allow[c] >> class_of[v] & 1),
+        which let the kernel mask 8 ids per lookup."""
+        if self.vocab_bits is None:
+            dev = self.class_of.device
+            V, C = self.class_of.numel(), self.allow.numel()
+            cls = self.class_of.to(torch.int64)
+            allow = self.allow.to(torch.int64) & 0xFFFFFFFF
+            ok = cls < C
+            allowed = ((allow.view(C, 1) >> cls.clamp(max=31).view(1, V)) & 1).bool() & ok.view(1, V)
+            words = (V + 31) // 32
+            padded = torch.zeros((C, words * 32), dtype=torch.int64, device=dev)
+            padded[:, :V] = allowed.to(torch.int64)
+            w = (padded.view(C, words, 32) << torch.arange(32, device=dev, dtype=torch.int64)).sum(-1)
+            w = torch.where(w >= 2**31, w - 2**32, w)
+            self.vocab_bits = w.to(torch.int32).contiguous()
+        return self.vocab_bits
 
     @classmethod
     def from_bool_table(cls, class_of, table, device) -> "GrammarTable":
@@ -182,6 +201,7 @@ class FusedSampler:
         if grammar is not None:
             a.grammar_class_of = grammar.class_of.data_ptr()
             a.grammar_allow = grammar.allow.data_ptr()
+            a.grammar_vocab_bits = grammar.bits().data_ptr()
             a.grammar_n_classes = grammar.allow.numel()
             a.prev_token = self.prev_token.data_ptr()
             a.flags |= N.FLAG_GRAMMAR_UPDATE_FROM_SAMPLE

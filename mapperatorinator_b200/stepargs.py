@@ -52,6 +52,7 @@ def fill_args(args: N.MtrSamplerArgs, s: StepInputs, addr: Callable[[str], int],
     if s.grammar_class_of is not None:
         args.grammar_class_of = addr("grammar_class_of")
         args.grammar_allow = addr("grammar_allow")
+        args.grammar_vocab_bits = addr("grammar_vocab_bits")
         args.grammar_n_classes = int(len(s.grammar_allow))
     args.prev_token = addr("prev_token")
     args.repetition_penalty = float(s.repetition_penalty)
@@ -95,6 +96,22 @@ def fill_args(args: N.MtrSamplerArgs, s: StepInputs, addr: Callable[[str], int],
     return args
 
 
+def grammar_vocab_bits(class_of: np.ndarray, allow: np.ndarray) -> np.ndarray:
+    """[C, ceil(V/32)] uint32: bit v of row c = (allow[c] >> class_of[v]) & 1."""
+    class_of = np.asarray(class_of, dtype=np.int64)
+    allow = np.asarray(allow, dtype=np.uint64)
+    V, C = len(class_of), len(allow)
+    ok = class_of < C
+    allowed = np.zeros((C, V), dtype=bool)
+    for c in range(C):
+        allowed[c] = ok & (((allow[c] >> np.minimum(class_of, 63).astype(np.uint64)) & np.uint64(1)) == 1)
+    words = (V + 31) // 32
+    padded = np.zeros((C, words * 32), dtype=bool)
+    padded[:, :V] = allowed
+    weights = (np.uint64(1) << np.arange(32, dtype=np.uint64))
+    return (padded.reshape(C, words, 32).astype(np.uint64) * weights).sum(-1).astype(np.uint32)
+
+
 def host_arrays(s: StepInputs) -> dict:
     """Named host arrays of a step (inputs, mutable state and outputs)."""
     B, V = s.num_rows, s.vocab
@@ -106,6 +123,8 @@ def host_arrays(s: StepInputs) -> dict:
     if s.grammar_class_of is not None:
         arr["grammar_class_of"] = np.ascontiguousarray(s.grammar_class_of, dtype=np.uint8)
         arr["grammar_allow"] = np.ascontiguousarray(s.grammar_allow, dtype=np.uint32)
+        if s.grammar_bits:
+            arr["grammar_vocab_bits"] = grammar_vocab_bits(s.grammar_class_of, s.grammar_allow)
     if s.prev_token is not None:
         arr["prev_token"] = np.array(s.prev_token, dtype=np.int32, copy=True)
     for i, (_t, _off, bits) in enumerate(s.cond):

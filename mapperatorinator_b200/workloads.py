@@ -65,6 +65,7 @@ class StepInputs:
     grammar_class_of: np.ndarray | None = None  # [V] uint8
     grammar_allow: np.ndarray | None = None     # [C] uint32
     prev_token: np.ndarray | None = None        # [B] int32
+    grammar_bits: bool = True                   # pass the per-class vocabulary bitmaps
     # penalties
     repetition_penalty: float = 1.0
     frequency_penalty: float = 0.0

@@ -183,6 +183,9 @@ static int cmp_float_desc(const void* pa, const void* pb) {
 
 static const float NEG_INF = -INFINITY;
 
+/* sizeof(MtrSamplerArgs) this oracle was compiled with (layout check). */
+size_t mtr_oracle_args_size(void) { return sizeof(MtrSamplerArgs); }
+
 /* Processes every row; host pointers throughout.  Returns 0. */
 int mtr_oracle_run(const MtrSamplerArgs* a) {
   const int64_t B = a->num_rows;

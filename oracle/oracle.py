@@ -25,18 +25,27 @@ _lib = None
 def build(force: bool = False) -> Path:
     src = ORACLE_DIR / "mtr_oracle.c"
     hdr = ORACLE_DIR.parent / "include" / "mtr_sampler.h"
-    if force or not LIB.exists() or LIB.stat().st_mtime < max(src.stat().st_mtime, hdr.stat().st_mtime):
+    if force or _stale():
         subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), "-B" if force else "_build/libmtr_oracle.so"],
                        check=True)
     return LIB
 
 
+def _stale() -> bool:
+    src = ORACLE_DIR / "mtr_oracle.c"
+    hdr = ORACLE_DIR.parent / "include" / "mtr_sampler.h"
+    return not LIB.exists() or LIB.stat().st_mtime < max(src.stat().st_mtime, hdr.stat().st_mtime)
+
+
 def load() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        if not LIB.exists():
+        if _stale():
             build()
         lib = ctypes.CDLL(str(LIB))
+        lib.mtr_oracle_args_size.restype = ctypes.c_size_t
+        if lib.mtr_oracle_args_size() != ctypes.sizeof(N.MtrSamplerArgs):
+            raise RuntimeError(f"oracle library {LIB} was built for another MtrSamplerArgs layout; rebuild it")
         lib.mtr_oracle_run.restype = ctypes.c_int
         lib.mtr_oracle_run.argtypes = [ctypes.POINTER(N.MtrSamplerArgs)]
         lib.mtr_oracle_expfx.restype = ctypes.c_uint32

@@ -130,13 +130,14 @@ def test_zero_rows_is_a_noop(lib):
     assert lib.mtr_sampler_launch(ctypes.byref(a), None) == N.OK
 
 
-@pytest.mark.parametrize("vocab,cs", [(1, 1), (4096, 1), (4097, 2), (8192, 2), (16384, 4), (65536, 8),
-                                      (131072, 8)])
-def test_query_geometry(lib, vocab, cs):
-    info = N.query(vocab, 10, True)
+@pytest.mark.parametrize("vocab,rows,cs", [(1, 10, 2), (4096, 10, 2), (4096, 1000, 1), (4097, 10, 2), (8192, 10, 2),
+                                           (16384, 10, 4), (65536, 10, 8), (131072, 10, 8)])
+def test_query_geometry(lib, vocab, rows, cs):
+    # few rows of a small vocabulary are split over a cluster pair (latency)
+    info = N.query(vocab, rows, True)
     assert info.cluster_size == cs
     assert info.threads * info.elems_per_thread * info.cluster_size >= vocab
-    assert info.grid == 10 * cs
+    assert info.grid == rows * cs
     assert info.candidate_cap == 256
     assert info.dyn_smem_bytes == info.threads * info.elems_per_thread * 10
 

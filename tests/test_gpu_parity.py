@@ -264,3 +264,23 @@ def test_cuda_graph_capture_replay(cuda_device):
     torch.cuda.synchronize()
     ref = oracle.run(s)
     assert np.array_equal(dev.results()["out_ids"], ref["out_ids"])
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_grammar_class_byte_path(cuda_device, dtype):
+    # the kernel masks from class bytes when no per-class vocabulary bitmap is given
+    s = W.batched_decode(seed=101, pairs=48, dtype=dtype).with_(grammar_bits=False, want_scores=True)
+    assert_parity(s, cuda_device)
+    s = W.sharded_decode(seed=102, pairs=64, dtype=dtype).with_(grammar_bits=False, want_scores=True)
+    assert_parity(s, cuda_device)
+
+
+def test_column_temperature_ranges_split_chunks(cuda_device):
+    # range edges inside 8-id chunks and overlapping ranges (first match wins)
+    rng = np.random.default_rng(111)
+    x = rng.normal(0, 2, size=(64, 4096)).astype(np.float32)
+    s = W.StepInputs(logits=W.bf16_bits(x), dtype="bf16", num_rows=64, temp_mode=N.TEMP_COLUMN_RANGES,
+                     temperature=1.3, col_ranges=[(3, 2003, 0.9), (1000, 1005, 0.5), (4090, 4096, 2.0)],
+                     select_mode=N.SELECT_SAMPLE, top_p=0.9, uniforms=rng.random(64, dtype=np.float32),
+                     want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
