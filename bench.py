@@ -236,6 +236,7 @@ def time_graph(fn_step, steps, stream, dist):
 # ---------------------------------------------------------------- our arm
 def run_ours(args, dist: Dist):
     from mapperatorinator_b200 import _native
+    from mapperatorinator_b200.parallel import shard_range
 
     _native.load()  # fail loudly without the native library
     device = torch.device("cuda", dist.local)
@@ -243,9 +244,8 @@ def run_ours(args, dist: Dist):
     if args.profile and args.profile_workload == "b64":
         run_b64(args, device, torch.cuda.Stream(device), dist, profile=args.profile)
         return
-    if PAIRS % dist.world:
-        raise SystemExit(f"{PAIRS} pairs do not split over {dist.world} GPUs")
-    pairs = PAIRS // dist.world
+    start, end = shard_range(PAIRS, dist.world, dist.rank)
+    pairs = end - start
     gen = torch.Generator(device).manual_seed(1234 + dist.rank)
     sampler = sharded_sampler(device, pairs, gen)
     history = torch.randint(0, VOCAB, (pairs, HISTORY), generator=gen, device=device)
