@@ -74,6 +74,7 @@ typedef enum MtrStatus {
 #define MTR_ROW_BAD_UNIFORM (1u << 3) /* uniform outside [0, 1) was clamped      */
 #define MTR_ROW_SLOW_PATH   (1u << 4) /* exact radix fallback was used (info)     */
 #define MTR_ROW_TIE_AT_CUT  (1u << 5) /* the top-p cut split equal scores (info)  */
+#define MTR_ROW_COPY_TIMEOUT (1u << 6) /* a staged row copy never landed; the rest of its CTA's rows were skipped */
 
 typedef enum MtrDType { MTR_DTYPE_F32 = 0, MTR_DTYPE_BF16 = 1, MTR_DTYPE_F16 = 2 } MtrDType;
 typedef enum MtrIdType { MTR_IDS_I64 = 0, MTR_IDS_I32 = 1 } MtrIdType;
@@ -108,6 +109,8 @@ typedef enum MtrSelect {
 #define MTR_FLAG_GRAMMAR_PREV_FROM_IDS      (1u << 2) /* previous token = input_ids[:, -1] instead of prev_token */
 #define MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE (1u << 3) /* prev_token[row] = emitted token after the draw        */
 #define MTR_FLAG_FORCE_RADIX                (1u << 4) /* test hook: always take the exact radix selection path  */
+#define MTR_FLAG_KERNEL_ROW_CTA             (1u << 5) /* use the row-per-CTA kernel (default: chosen by shape)  */
+#define MTR_FLAG_KERNEL_ROW_WARP            (1u << 6) /* use the row-per-warp kernel (V <= 4096, <= 32767 penalty ids) */
 
 /*
  * All pointer fields are device pointers (host pointers for the CPU oracle
@@ -208,6 +211,7 @@ typedef struct MtrLaunchInfo {
   int32_t max_vocab;      /* MTR_MAX_VOCAB */
   int32_t max_ids_len;    /* MTR_MAX_IDS_LEN */
   int32_t candidate_cap;  /* size of the exact in-bin candidate list */
+  int32_t kernel;         /* 0: row-per-CTA (cluster) kernel, 1: row-per-warp kernel */
 } MtrLaunchInfo;
 
 /* ABI identity: MTR_ABI_VERSION and sizeof(MtrSamplerArgs) of the library. */
@@ -220,8 +224,13 @@ int mtr_args_init(MtrSamplerArgs* args);
 /* Host-side argument checks only (no CUDA call). */
 int mtr_sampler_validate(const MtrSamplerArgs* args);
 
-/* Geometry the launcher would use for (vocab, num_rows, penalties on/off). */
+/* Row-per-CTA geometry for (vocab, num_rows, penalties on/off). */
 int mtr_sampler_query(int32_t vocab, int32_t num_rows, int32_t with_penalties, MtrLaunchInfo* out);
+
+/* Kernel and geometry mtr_sampler_launch would use for these exact arguments
+ * (validates them first).  The row-per-warp kernel is chosen for >= 2 rows per
+ * SM of a vocabulary <= 4096 whose selection is argmax or a top-k <= 128. */
+int mtr_sampler_query_args(const MtrSamplerArgs* args, MtrLaunchInfo* out);
 
 /*
  * Validate and enqueue the fused step on `stream` (a cudaStream_t; NULL = the

@@ -43,6 +43,7 @@ ROW_BAD_ID = 1 << 2
 ROW_BAD_UNIFORM = 1 << 3
 ROW_SLOW_PATH = 1 << 4
 ROW_TIE_AT_CUT = 1 << 5
+ROW_COPY_TIMEOUT = 1 << 6
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 IDS_I64, IDS_I32 = 0, 1
@@ -56,6 +57,8 @@ FLAG_MONO_UPDATE_FROM_SAMPLE = 1 << 1
 FLAG_GRAMMAR_PREV_FROM_IDS = 1 << 2
 FLAG_GRAMMAR_UPDATE_FROM_SAMPLE = 1 << 3
 FLAG_FORCE_RADIX = 1 << 4
+FLAG_KERNEL_ROW_CTA = 1 << 5
+FLAG_KERNEL_ROW_WARP = 1 << 6
 
 
 class MtrSamplerArgs(ctypes.Structure):
@@ -132,7 +135,12 @@ class MtrLaunchInfo(ctypes.Structure):
         ("max_vocab", c_int32),
         ("max_ids_len", c_int32),
         ("candidate_cap", c_int32),
+        ("kernel", c_int32),
     ]
+
+
+KERNEL_ROW_CTA = 0
+KERNEL_ROW_WARP = 1
 
 
 # Every symbol include/mtr_sampler.h declares: (name, restype, argtypes).
@@ -142,6 +150,7 @@ EXPORTS = {
     "mtr_args_init": (ctypes.c_int, [ctypes.POINTER(MtrSamplerArgs)]),
     "mtr_sampler_validate": (ctypes.c_int, [ctypes.POINTER(MtrSamplerArgs)]),
     "mtr_sampler_query": (ctypes.c_int, [c_int32, c_int32, c_int32, ctypes.POINTER(MtrLaunchInfo)]),
+    "mtr_sampler_query_args": (ctypes.c_int, [ctypes.POINTER(MtrSamplerArgs), ctypes.POINTER(MtrLaunchInfo)]),
     "mtr_sampler_launch": (ctypes.c_int, [ctypes.POINTER(MtrSamplerArgs), c_void_p]),
     "mtr_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "mtr_last_cuda_error": (ctypes.c_int, []),
@@ -238,4 +247,11 @@ def launch(args: MtrSamplerArgs, stream: int | None) -> None:
 def query(vocab: int, num_rows: int, with_penalties: bool = False) -> MtrLaunchInfo:
     info = MtrLaunchInfo()
     check(load().mtr_sampler_query(vocab, num_rows, int(with_penalties), ctypes.byref(info)), "mtr_sampler_query")
+    return info
+
+
+def query_args(args: MtrSamplerArgs) -> MtrLaunchInfo:
+    """Kernel and geometry the launcher picks for these exact arguments."""
+    info = MtrLaunchInfo()
+    check(load().mtr_sampler_query_args(ctypes.byref(args), ctypes.byref(info)), "mtr_sampler_query_args")
     return info

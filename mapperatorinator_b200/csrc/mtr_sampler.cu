@@ -204,6 +204,27 @@ __device__ __forceinline__ int dbin(float mx, float x) {
 
 __device__ __forceinline__ bool finite_val(float x) { return fabsf(x) < pos_inf(); }
 
+// maxima that return NaN when any input is NaN (three-input form: sm_100)
+__device__ __forceinline__ float fmax3n(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmax2n(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+// Hint: pull [p, p + bytes) into L2 with one bulk prefetch (16-byte granules
+// fully inside the range; nothing is read into the SM).
+__device__ __forceinline__ void l2_prefetch(const void* p, size_t bytes) {
+  const uintptr_t b0 = ((uintptr_t)p + 15u) & ~(uintptr_t)15u;
+  const uintptr_t b1 = ((uintptr_t)p + bytes) & ~(uintptr_t)15u;
+  if (b1 > b0 && b1 - b0 < (1u << 20))
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b0), "r"((uint32_t)(b1 - b0)) : "memory");
+}
+
 // canonical order: higher score first, then lower token id
 __device__ __forceinline__ bool canon_before(float xj, int32_t ij, float xi, int32_t ii) {
   return xj > xi || (xj == xi && ij < ii);
@@ -220,7 +241,29 @@ template <> struct Elem<float> {
     return __uint_as_float(v);
   }
   __device__ static float one(const void* p, int64_t i) { return __ldcs((const float*)p + i); }
+  // the 16-byte group starting at element i from scalar loads (ids >= V read as 0)
+  __device__ static uint4 gather(const void* p, int i, int V) {
+    const float* f = (const float*)p;
+    uint4 r;
+    r.x = i < V ? __float_as_uint(__ldcs(f + i)) : 0u;
+    r.y = i + 1 < V ? __float_as_uint(__ldcs(f + i + 1)) : 0u;
+    r.z = i + 2 < V ? __float_as_uint(__ldcs(f + i + 2)) : 0u;
+    r.w = i + 3 < V ? __float_as_uint(__ldcs(f + i + 3)) : 0u;
+    return r;
+  }
 };
+// 16-bit types: the 16-byte group of 8 elements from scalar loads (ids >= V read as 0)
+__device__ __forceinline__ uint4 gather_u16(const void* p, int i, int V) {
+  const unsigned short* h = (const unsigned short*)p;
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t lo = i + 2 * k < V ? (uint32_t)__ldcs(h + i + 2 * k) : 0u;
+    const uint32_t hi = i + 2 * k + 1 < V ? (uint32_t)__ldcs(h + i + 2 * k + 1) : 0u;
+    w[k] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
 template <> struct Elem<__nv_bfloat16> {
   static constexpr int VEC = 8;
   __device__ static float get(const uint4& w, int e) {
@@ -231,6 +274,7 @@ template <> struct Elem<__nv_bfloat16> {
     const unsigned short h = __ldcs((const unsigned short*)p + i);
     return __uint_as_float((uint32_t)h << 16);
   }
+  __device__ static uint4 gather(const void* p, int i, int V) { return gather_u16(p, i, V); }
 };
 template <> struct Elem<__half> {
   static constexpr int VEC = 8;
@@ -243,6 +287,7 @@ template <> struct Elem<__half> {
     const unsigned short h = __ldcs((const unsigned short*)p + i);
     return __half2float(__ushort_as_half(h));
   }
+  __device__ static uint4 gather(const void* p, int i, int V) { return gather_u16(p, i, V); }
 };
 
 __device__ __forceinline__ int64_t load_id(const MtrSamplerArgs& a, int64_t row, int64_t pos) {
@@ -456,6 +501,9 @@ struct Derived {
   float temp_rcp;
   float cond_rcp[MTR_MAX_COND_TEMPS];
   float col_rcp[MTR_MAX_COL_TEMP_RANGES];
+  // -1, -0 and 1 as launch parameters: FMAs with them stay FMAs (a compile-time
+  // constant would let the compiler turn them into a mul + add pair and fuse it)
+  float neg_one, neg_zero, one;
 };
 
 // Push the elements of this thread whose bit is set in `mask` to the local
@@ -1671,6 +1719,1096 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
 }
 
 // ---------------------------------------------------------------------------
+// row-per-warp kernel: many rows of a vocabulary <= 4096
+//
+// One warp owns one row at a time and walks rows r, r + grid, ... (persistent
+// grid sized by occupancy).  The row's logits arrive in shared memory by bulk
+// asynchronous copies (cp.async.bulk, completion on an mbarrier) and are
+// processed in place into the fp32 row X; the next row's copy is issued as soon
+// as X is no longer needed (normally right after the top-k survivors are
+// listed), so it lands while the current row finishes its top-p and draw.  No
+// block barrier exists: cross-lane steps are shuffles, ballots and __syncwarp.
+//
+// X layout.  16-bit logits: chunk c (ids 8c .. 8c+7) keeps ids 8c..8c+3 at
+// floats [4c, 4c+4) and ids 8c+4..8c+7 at [VP/2 + 4c, ...).  The raw first-half
+// row is copied to bytes [0, 2V) and the raw second-half row to [2VP, 2VP+2V),
+// so chunk c's raw data sits exactly where its processed floats go.  fp32
+// logits: natural layout (id i at float i), the raw row copied in place.
+//
+// Dynamic shared memory per warp: X (VP floats) + a region that holds the u16
+// history counts during the chain and the selection state after it.
+// ---------------------------------------------------------------------------
+constexpr int WV_MAX = 4096;
+constexpr int WNB = 256;               // histogram bins
+constexpr float WBIN_SCALE = 8.0f;     // chunk-maximum bins per logit
+constexpr int WCAP = 256;              // candidate / survivor list
+constexpr int WMINI = 64;              // crossing-bin list
+constexpr int WHIST = 16;              // history ids per lane held in registers
+constexpr int WSEL_BYTES = WNB * 8 + WCAP * 12 + WMINI * 12 + 16;
+constexpr int WMAX_PEN_IDS = 32767;    // counts keep a claim bit in bit 15
+constexpr uint32_t WAIT_POLLS = 1u << 20;  // ~1 s of 1 us suspends before a copy counts as lost
+
+__host__ __device__ constexpr int warp_vpad(int V) { return (V + 255) / 256 * 256; }
+__host__ __device__ constexpr int warp_union_bytes(int V) {
+  return warp_vpad(V) * 2 > WSEL_BYTES ? warp_vpad(V) * 2 : WSEL_BYTES;
+}
+__host__ __device__ constexpr int warp_bytes(int V) { return warp_vpad(V) * 4 + warp_union_bytes(V); }
+
+__device__ __forceinline__ int wbin(float mx, float x) {
+  float s = __fmul_rn(__fsub_rn(mx, x), WBIN_SCALE);
+  s = fminf(s, (float)(WNB - 1));
+  return __float2int_rz(s);
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* m) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_addr(m)) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* m, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(m)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* m, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(m)), "r"(parity), "r"(1000u)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait for phase `parity`; false when the copy did not land in time
+__device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
+  for (uint32_t i = 0; i < WAIT_POLLS; ++i)
+    if (mbar_try_wait(m, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* m) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(m))
+               : "memory");
+}
+// order this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) writes to it
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Crossing of `lim` in a 256-bin histogram h (lane owns bins 8*lane .. 8*lane+7):
+// the bin b with W(bins < b) <= lim < W(bins <= b).  Returns -1 when lim >= total.
+template <typename W>
+__device__ __forceinline__ int warp_crossing(const W* h, u64 lim, int lane, u64& above, u64& w) {
+  W v[8];
+  if constexpr (sizeof(W) == 4) {
+    const uint4 p0 = *(const uint4*)(h + lane * 8), p1 = *(const uint4*)(h + lane * 8 + 4);
+    v[0] = p0.x; v[1] = p0.y; v[2] = p0.z; v[3] = p0.w;
+    v[4] = p1.x; v[5] = p1.y; v[6] = p1.z; v[7] = p1.w;
+  } else {
+#pragma unroll
+    for (int r = 0; r < 8; r += 2) {
+      const ulonglong2 p = *(const ulonglong2*)(h + lane * 8 + r);
+      v[r] = p.x;
+      v[r + 1] = p.y;
+    }
+  }
+  u64 s = 0;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) s += v[r];
+  const u64 incl = warp_incl_scan_u64(s, lane);
+  int my_b = -1;
+  u64 my_above = 0, my_w = 0;
+  if (incl - s <= lim && lim < incl) {
+    u64 c = incl - s;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (my_b < 0 && c + v[r] > lim) {
+        my_b = lane * 8 + r;
+        my_above = c;
+        my_w = v[r];
+      }
+      c += v[r];
+    }
+  }
+  const unsigned bal = __ballot_sync(FULL, my_b >= 0);
+  if (!bal) return -1;
+  const int src = __ffs(bal) - 1;
+  above = __shfl_sync(FULL, my_above, src);
+  w = __shfl_sync(FULL, my_w, src);
+  return __shfl_sync(FULL, my_b, src);
+}
+
+// x / t for a chunk (y = RN(1/t)): Markstein on pairs when every value that is
+// not -inf lies in [2^-60, 2^60) (-inf passes through), the IEEE divide per
+// element otherwise.
+__device__ __forceinline__ void div_chunk(float (&v)[8], float t, float y) {
+  float w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = v[e] == neg_inf() ? 1.0f : fabsf(v[e]);
+  const float amax = fmax3n(fmax3n(w[0], w[1], w[2]), fmax3n(w[3], w[4], w[5]), fmax2n(w[6], w[7]));
+  const float amin = fminf(fminf(fminf(w[0], w[1]), fminf(w[2], w[3])), fminf(fminf(w[4], w[5]), fminf(w[6], w[7])));
+  if (amax < 0x1p60f && amin >= 0x1p-60f) {
+    const u64 Y = pk2(y, y), NT = pk2(-t, -t);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const u64 Xv = pk2(v[e], v[e + 1]);
+      const u64 Q0 = mul2(Xv, Y);
+      float q0, q1;
+      up2(fma2(fma2(Q0, NT, Xv), Y, Q0), q0, q1);
+      v[e] = v[e] == neg_inf() ? v[e] : q0;
+      v[e + 1] = v[e + 1] == neg_inf() ? v[e + 1] : q1;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = div_by(v[e], t, y);
+  }
+}
+
+// temperature of a chunk: the row's (scalar / conditional) or the column ranges'
+// (first match wins; a chunk split by a range edge goes element by element)
+__device__ __forceinline__ void temp_chunk(const MtrSamplerArgs& a, const Derived& dv, float (&v)[8], int id0,
+                                           float t_row, float y_row) {
+  if (a.temp_mode != MTR_TEMP_COLUMN_RANGES) {
+    if (t_row != 1.0f) div_chunk(v, t_row, y_row);
+    return;
+  }
+  float t0 = a.temperature, y0 = dv.temp_rcp, t1 = a.temperature;
+  bool uniform_chunk = true;
+  for (int r = a.n_col_ranges - 1; r >= 0; --r) {
+    const int cs = a.col_start[r], ce = a.col_end[r];
+    if (id0 >= cs && id0 < ce) {
+      t0 = a.col_temperature[r];
+      y0 = dv.col_rcp[r];
+    }
+    if (id0 + 7 >= cs && id0 + 7 < ce) t1 = a.col_temperature[r];
+    if ((cs > id0 && cs < id0 + 8) || (ce > id0 && ce < id0 + 8)) uniform_chunk = false;
+  }
+  if (uniform_chunk && t0 == t1) {
+    if (t0 != 1.0f) div_chunk(v, t0, y0);
+    return;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float te = a.temperature, ye = dv.temp_rcp;
+    for (int r = a.n_col_ranges - 1; r >= 0; --r)
+      if (id0 + e >= a.col_start[r] && id0 + e < a.col_end[r]) {
+        te = a.col_temperature[r];
+        ye = dv.col_rcp[r];
+      }
+    if (te != 1.0f) v[e] = div_by(v[e], te, ye);
+  }
+}
+
+// per-row values loaded one row ahead (independent loads only)
+struct WarpAhead {
+  int32_t hid[WHIST];  // ids at positions hbase + lane + 32k (INT32_MIN: outside int32)
+  int32_t hbase;
+  int64_t s0;          // lane 0: mono_state; lane 1: previous token; lane 2/3 unused
+  int64_t s1;          // lane 0: last id (mono update); lane 3: uniform bits
+  int64_t cond[MTR_MAX_COND_TEMPS];  // lane 2: ids at L - cond_offset[c]
+};
+
+__device__ __forceinline__ int32_t narrow_id(int64_t t) {
+  return (t >= INT32_MIN && t <= INT32_MAX) ? (int32_t)t : INT32_MIN;
+}
+
+__device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derived& dv, int64_t row, int lane, int L,
+                                           WarpAhead& w) {
+  w.hbase = L > WHIST * 32 ? L - WHIST * 32 : 0;
+  const bool need_hist = dv.pen_on || a.mono_mode == MTR_MONO_SCAN;
+#pragma unroll
+  for (int k = 0; k < WHIST; ++k) {
+    const int pos = w.hbase + lane + 32 * k;
+    w.hid[k] = (need_hist && pos < L) ? narrow_id(load_id(a, row, pos)) : INT32_MIN;
+  }
+  w.s0 = 0;
+  w.s1 = 0;
+  if (lane == 0) {
+    if (a.mono_mode == MTR_MONO_STATE) w.s0 = a.mono_state[row];
+    if (L > 0 && (a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS)) w.s1 = load_id(a, row, L - 1);
+  } else if (lane == 1) {
+    w.s0 = -1;
+    if (a.grammar_class_of) {
+      if (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) w.s0 = L > 0 ? load_id(a, row, L - 1) : -1;
+      else if (a.prev_token) w.s0 = a.prev_token[row];
+    }
+  } else if (lane == 3) {
+    if (a.select_mode == MTR_SELECT_SAMPLE) w.s1 = (int64_t)__float_as_uint(a.uniforms[row]);
+  }
+#pragma unroll
+  for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c) {
+    w.cond[c] = -1;
+    if (lane == 2 && a.temp_mode == MTR_TEMP_ROW_CONDITIONAL && c < a.n_cond) {
+      const int off = a.cond_offset[c];
+      if (off >= 1 && L >= off) w.cond[c] = load_id(a, row, L - off);
+    }
+  }
+}
+
+template <typename Tin, bool CFG>
+__global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__ MtrSamplerArgs a,
+                                                         const __grid_constant__ Derived dv) {
+  using E = Elem<Tin>;
+  constexpr int VEC = E::VEC;            // elements per 16-byte group
+  constexpr int NV = 8 / VEC;            // 16-byte groups per 8-id chunk and side
+  constexpr bool SPLIT = sizeof(Tin) == 2;
+  constexpr int NS = WV_MAX / 256;       // chunk slots per lane
+  __shared__ __align__(8) uint64_t mbar;
+  extern __shared__ __align__(16) uint8_t dsm[];
+  const int lane = threadIdx.x;
+  const int V = a.vocab;
+  const int VP = warp_vpad(V);
+  const int HALF = VP / 2;
+  const int nch = (V + 7) / 8;
+  float* X = (float*)dsm;
+  uint8_t* U = dsm + (size_t)VP * 4;
+  uint32_t* cnt = (uint32_t*)U;          // chain: u16 history counts (bit 15 = claimed), two per word
+  u64* hist = (u64*)U;                   // selection
+  uint32_t* hc = (uint32_t*)U;
+  float* lx = (float*)(U + WNB * 8);
+  int32_t* lid = (int32_t*)(lx + WCAP);
+  uint32_t* lq = (uint32_t*)(lid + WCAP);
+  float* mx = (float*)(lq + WCAP);
+  int32_t* mi = (int32_t*)(mx + WMINI);
+  uint32_t* mq = (uint32_t*)(mi + WMINI);
+  const int L = a.input_ids ? dv.ids_len : 0;
+  const float NEG = neg_inf();
+  const int sel = a.select_mode;
+  const bool force_radix = (a.flags & MTR_FLAG_FORCE_RADIX) != 0;
+  const bool bulk = dv.vec_ok != 0;
+  const uint32_t row_bytes = (uint32_t)V * (uint32_t)sizeof(Tin);
+  const u64 NEG1 = pk2(dv.neg_one, dv.neg_one), NZ = pk2(dv.neg_zero, dv.neg_zero), ONE = pk2(dv.one, dv.one);
+  const u64 SC = pk2(a.cfg_scale, a.cfg_scale);
+  const bool pen_temp = dv.pen_on && (a.temp_mode == MTR_TEMP_COLUMN_RANGES || a.temp_mode == MTR_TEMP_ROW_CONDITIONAL ||
+                                      a.temperature != 1.0f);
+
+  auto lo_of = [&](int c) -> float* { return X + (SPLIT ? 4 * c : 8 * c); };
+  auto hi_of = [&](int c) -> float* { return X + (SPLIT ? HALF + 4 * c : 8 * c + 4); };
+  auto xat = [&](int id) -> float* { return ((id & 4) ? hi_of(id >> 3) : lo_of(id >> 3)) + (id & 3); };
+  auto issue_copy = [&](int64_t r) {  // lane 0; every lane fenced, then __syncwarp
+    const Tin* s1 = (const Tin*)a.logits + r * a.logits_row_stride;
+    mbar_expect_tx(&mbar, (SPLIT && CFG) ? 2u * row_bytes : row_bytes);
+    bulk_g2s(X, s1, row_bytes, &mbar);
+    if constexpr (SPLIT && CFG) bulk_g2s(X + HALF, s1 + dv.second * a.logits_row_stride, row_bytes, &mbar);
+  };
+
+  if (lane == 0) mbar_init(&mbar);
+  __syncwarp();
+  int64_t row = blockIdx.x;
+  uint32_t parity = 0;
+  if (bulk && lane == 0 && row < a.num_rows) issue_copy(row);
+  WarpAhead ah;
+  if (row < a.num_rows) load_ahead(a, dv, row, lane, L, ah);
+
+#pragma unroll 1
+  for (; row < a.num_rows; row += gridDim.x) {
+    const int64_t nrow = row + gridDim.x;
+    bool issued = false;
+    auto issue_next = [&]() {
+      if (issued) return;
+      issued = true;
+      fence_proxy_async();
+      __syncwarp();
+      if (bulk && lane == 0 && nrow < a.num_rows) issue_copy(nrow);
+    };
+    const Tin* r1 = (const Tin*)a.logits + row * a.logits_row_stride;
+    const Tin* r2 = r1 + dv.second * a.logits_row_stride;
+
+    // ---------------------------------------------------------- row scalars (dependent loads from the ahead values)
+    uint32_t status = 0;
+    int32_t mono = -1;
+    uint32_t allow = 0xffffffffu;
+    int gon = 0;
+    const uint32_t* gbits = nullptr;
+    float t_row = a.temperature, y_row = dv.temp_rcp, u = 0.0f;
+    {
+      int32_t m0 = -1;
+      uint32_t al = 0xffffffffu, st = 0;
+      int g = 0;
+      u64 gb = 0;
+      float t = a.temperature, y = dv.temp_rcp, uu = 0.0f;
+      if (lane == 0 && a.mono_mode == MTR_MONO_STATE) {
+        m0 = (int32_t)ah.s0;
+        if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) m0 = mono_update(a, m0, ah.s1);
+      } else if (lane == 1 && a.grammar_class_of) {
+        const int64_t prev = ah.s0;
+        if (prev >= V) st |= MTR_ROW_BAD_ID;
+        if (prev >= 0 && prev < V) {
+          const uint32_t c = __ldg(a.grammar_class_of + prev);
+          if (c < (uint32_t)a.grammar_n_classes) {
+            g = 1;
+            al = __ldg(a.grammar_allow + c);
+            if (a.grammar_vocab_bits) gb = (u64)(a.grammar_vocab_bits + (size_t)c * dv.gwords);
+          } else {
+            st |= MTR_ROW_BAD_ID;
+          }
+        }
+      } else if (lane == 2 && a.temp_mode == MTR_TEMP_ROW_CONDITIONAL) {
+        for (int c = 0; c < a.n_cond; ++c) {
+          const int64_t tok = ah.cond[c];
+          if (tok >= 0 && tok < V && ((__ldg(a.cond_token_bits[c] + (tok >> 5)) >> (tok & 31)) & 1u)) {
+            t = a.cond_temperature[c];
+            y = dv.cond_rcp[c];
+            break;
+          }
+        }
+      } else if (lane == 3 && sel == MTR_SELECT_SAMPLE) {
+        uu = __uint_as_float((uint32_t)ah.s1);
+        if (!(uu >= 0.0f)) {
+          uu = 0.0f;
+          st |= MTR_ROW_BAD_UNIFORM;
+        } else if (uu >= 1.0f) {
+          uu = 0x1.fffffep-1f;
+          st |= MTR_ROW_BAD_UNIFORM;
+        }
+      }
+      if (a.mono_mode == MTR_MONO_STATE) mono = __shfl_sync(FULL, m0, 0);
+      allow = __shfl_sync(FULL, al, 1);
+      gon = __shfl_sync(FULL, g, 1);
+      gbits = (const uint32_t*)__shfl_sync(FULL, gb, 1);
+      t_row = __shfl_sync(FULL, t, 2);
+      y_row = __shfl_sync(FULL, y, 2);
+      u = __shfl_sync(FULL, uu, 3);
+      status = __reduce_or_sync(FULL, st);
+    }
+    if (a.mono_mode == MTR_MONO_SCAN) {
+      // last time-shift position and last start-of-sequence position
+      int lts = -1, lsos = -1;
+      int32_t lts_id = 0;
+#pragma unroll
+      for (int k = 0; k < WHIST; ++k) {
+        const int pos = ah.hbase + lane + 32 * k;
+        const int32_t t = ah.hid[k];
+        if (pos < L && t != INT32_MIN) {
+          if (t >= a.ts_start && t < a.ts_end) {
+            lts = pos;
+            lts_id = t;
+          }
+          if (is_sos(a, t)) lsos = pos;
+        }
+      }
+      for (int base = ah.hbase - 32; base > -32 && __all_sync(FULL, lts < 0 && lsos < 0); base -= 32) {
+        // neither seen in the register window: walk back (long histories only)
+        const int pos = base + lane;
+        if (pos >= 0) {
+          const int64_t t = load_id(a, row, pos);
+          if (t >= a.ts_start && t < a.ts_end) {
+            lts = pos;
+            lts_id = (int32_t)t;
+          }
+          if (is_sos(a, t)) lsos = pos;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const int op = __shfl_xor_sync(FULL, lts, o);
+        const int32_t oid = __shfl_xor_sync(FULL, lts_id, o);
+        if (op > lts) {
+          lts = op;
+          lts_id = oid;
+        }
+        lsos = max(lsos, __shfl_xor_sync(FULL, lsos, o));
+      }
+      mono = (lts != -1 && lts > lsos) ? lts_id - a.ts_start : -1;
+    }
+    const int mono_hi = mono >= 0 ? (int32_t)min((int64_t)a.ts_end, (int64_t)a.ts_start + mono) : -1;
+    const bool masks = mono_hi > a.ts_start || gon || (V & 7) != 0;
+
+    // ---------------------------------------------------------- history counts
+    if (dv.pen_on) {
+      for (int i = lane * 4; i < VP / 2; i += 128) *(uint4*)(cnt + i) = make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+      uint32_t bad = 0;
+#pragma unroll
+      for (int k = 0; k < WHIST; ++k) {
+        const int pos = ah.hbase + lane + 32 * k;
+        const int32_t t = ah.hid[k];
+        if (pos >= a.penalty_start && pos < L) {
+          if (t < 0 || t >= V) bad = 1;
+          else atomicAdd(cnt + (t >> 1), 1u << (16 * (t & 1)));
+        }
+      }
+      for (int pos = a.penalty_start + lane; pos < ah.hbase; pos += 32) {  // long histories only
+        const int64_t t = load_id(a, row, pos);
+        if (t < 0 || t >= V) bad = 1;
+        else atomicAdd(cnt + (t >> 1), 1u << (16 * (t & 1)));
+      }
+      if (__any_sync(FULL, bad)) status |= MTR_ROW_BAD_ID;
+      __syncwarp();
+    }
+
+    // ---------------------------------------------------------- this row's logits
+    bool lost = false;
+    if (bulk) {
+      lost = !mbar_wait(&mbar, parity);
+      parity ^= 1u;
+      if (__any_sync(FULL, lost)) {
+        if (lane == 0 && a.out_status) a.out_status[row] = status | MTR_ROW_COPY_TIMEOUT;
+        mbar_wait(&mbar, parity ^ 1u);  // bounded: a late copy still owns X
+        return;
+      }
+    }
+
+    // ---------------------------------------------------------- pass 1 (in place): CFG, bias, [temperature], masks
+    // Masks only ever write -inf, which bias, penalties and temperature map to
+    // -inf again, so the order here (masks before or after temperature)
+    // reproduces CFG -> masks -> bias -> penalties -> temperature exactly.
+#pragma unroll 1
+    for (int s = 0; s < NS; ++s) {
+      const int c = s * 32 + lane;
+      const int id0 = c * 8;
+      if (id0 >= V) break;
+      uint4 ra[NV];
+#pragma unroll
+      for (int h = 0; h < NV; ++h) {
+        if (bulk) ra[h] = *(const uint4*)(lo_of(c) + 4 * h);
+        else ra[h] = E::gather(r1, id0 + h * VEC, V);
+      }
+      float v[8];
+      if constexpr (CFG) {
+        uint4 rb[NV];
+#pragma unroll
+        for (int h = 0; h < NV; ++h) {
+          if (SPLIT && bulk) rb[h] = *(const uint4*)(hi_of(c) + 4 * h);
+          else if (bulk) rb[h] = __ldcs((const uint4*)(r2 + id0 + h * VEC));
+          else rb[h] = E::gather(r2, id0 + h * VEC, V);
+        }
+        // b + (a - b) * s as three FMAs whose -1 / -0 / 1 operands are launch
+        // parameters, so the compiler cannot form a fusable mul + add pair
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const u64 A = pk2(E::get(ra[e / VEC], e % VEC), E::get(ra[e / VEC], e % VEC + 1));
+          const u64 B = pk2(E::get(rb[e / VEC], e % VEC), E::get(rb[e / VEC], e % VEC + 1));
+          up2(fma2(fma2(fma2(B, NEG1, A), SC, NZ), ONE, B), v[e], v[e + 1]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = E::get(ra[e / VEC], e % VEC);
+      }
+      if (a.timeshift_bias != 0.0f) {
+        const uint32_t bb = range_bits(a.ts_start - id0, a.ts_end - id0);
+        if (bb) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if ((bb >> e) & 1u) v[e] = __fadd_rn(v[e], a.timeshift_bias);
+        }
+      }
+      if (!dv.pen_on) temp_chunk(a, dv, v, id0, t_row, y_row);
+      if (masks) {
+        uint32_t keep = range_bits(0, V - id0) & ~range_bits(a.ts_start - id0, mono_hi - id0);
+        if (gon) {
+          if (gbits) {
+            keep &= __ldg(gbits + (id0 >> 5)) >> (id0 & 31);
+          } else {
+            uint32_t g = 0;
+            const uint32_t ncls = (uint32_t)a.grammar_n_classes;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if (id0 + e < V) {
+                const uint32_t cl = __ldg(a.grammar_class_of + id0 + e);
+                g |= (cl < ncls ? (allow >> cl) & 1u : 0u) << e;
+              }
+            }
+            keep &= g;
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = ((keep >> e) & 1u) ? v[e] : NEG;
+      }
+      *(float4*)lo_of(c) = make_float4(v[0], v[1], v[2], v[3]);
+      *(float4*)hi_of(c) = make_float4(v[4], v[5], v[6], v[7]);
+    }
+
+    // ---------------------------------------------------------- penalties: one lane per distinct history id
+    if (dv.pen_on) {
+      __syncwarp();
+      const float rp = a.repetition_penalty, fp = a.frequency_penalty, pp = a.presence_penalty;
+      auto apply = [&](int32_t t) {
+        const uint32_t sh = 16u * (uint32_t)(t & 1);
+        const uint32_t old = atomicOr(cnt + (t >> 1), 0x8000u << sh);
+        if ((old >> sh) & 0x8000u) return;  // another lane owns this id
+        const float c = (float)((old >> sh) & 0x7fffu);
+        float* p = xat(t);
+        float x = *p;
+        if (rp != 1.0f) x = x < 0.0f ? __fmul_rn(x, rp) : __fdiv_rn(x, rp);
+        if (fp != 0.0f) x = __fsub_rn(x, __fmul_rn(fp, c));
+        if (pp != 0.0f) x = __fsub_rn(x, pp);
+        *p = x;
+      };
+#pragma unroll
+      for (int k = 0; k < WHIST; ++k) {
+        const int pos = ah.hbase + lane + 32 * k;
+        const int32_t t = ah.hid[k];
+        if (pos >= a.penalty_start && pos < L && t >= 0 && t < V) apply(t);
+      }
+      for (int pos = a.penalty_start + lane; pos < ah.hbase; pos += 32) {  // long histories only
+        const int64_t t = load_id(a, row, pos);
+        if (t >= 0 && t < V) apply((int32_t)t);
+      }
+      __syncwarp();
+      if (pen_temp) {
+#pragma unroll 1
+        for (int s = 0; s < NS; ++s) {
+          const int c = s * 32 + lane;
+          const int id0 = c * 8;
+          if (id0 >= V) break;
+          const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+          float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+          temp_chunk(a, dv, v, id0, t_row, y_row);
+          *(float4*)lo_of(c) = make_float4(v[0], v[1], v[2], v[3]);
+          *(float4*)hi_of(c) = make_float4(v[4], v[5], v[6], v[7]);
+        }
+      }
+    }
+    __syncwarp();
+
+    // ---------------------------------------------------------- chunk maxima (NaN propagates)
+    float cm[NS];
+    float lmax = NEG;
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      const int c = s * 32 + lane;
+      cm[s] = NEG;
+      if (c < nch) {
+        const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+        cm[s] = fmax3n(fmax3n(f0.x, f0.y, f0.z), fmax3n(f0.w, f1.x, f1.y), fmax2n(f1.z, f1.w));
+        lmax = fmax2n(lmax, cm[s]);
+      }
+    }
+    float gmax = lmax;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) gmax = fmax2n(gmax, __shfl_xor_sync(FULL, gmax, o));
+    const bool has_nan = gmax != gmax;
+    const bool nonfinite = has_nan || gmax == pos_inf();
+    const bool all_masked = !nonfinite && gmax == NEG;
+    if (nonfinite) status |= MTR_ROW_NONFINITE;
+    if (all_masked) status |= MTR_ROW_ALL_MASKED;
+    const bool clean = !nonfinite && !all_masked;
+    const bool want_lp = a.out_logprobs != nullptr;
+    const bool need_x_late = a.out_scores != nullptr || want_lp;
+    const bool need_mass = clean && (sel == MTR_SELECT_SAMPLE || want_lp || (sel == MTR_SELECT_NONE && dv.topp_on));
+
+    float tk = NEG;
+    bool topp_cut = false;
+    float cut_x = 0.0f;
+    int32_t cut_id = NO_ID;
+    u64 qkept = 0;
+    int32_t token = -1;
+    int n = -1;  // survivors listed in lx / lid (-1: no list)
+
+    if (sel == MTR_SELECT_ARGMAX && !all_masked) {
+      // lowest id of the maximum (of the first NaN when there is one)
+      int32_t myc = NO_ID;
+#pragma unroll
+      for (int s = NS - 1; s >= 0; --s)
+        if (has_nan ? cm[s] != cm[s] : cm[s] == gmax) myc = s * 32 + lane;
+      myc = __reduce_min_sync(FULL, myc);
+      int32_t hit = NO_ID;
+      if (myc < nch && lane < 8) {
+        const int id = myc * 8 + lane;
+        const float v = *xat(id);
+        if (has_nan ? v != v : v == gmax) hit = id;
+      }
+      token = __reduce_min_sync(FULL, hit);
+      if (token == NO_ID) token = 0;
+    } else if (sel == MTR_SELECT_ARGMAX) {
+      token = 0;
+    } else if (clean && dv.topk_on) {
+      const uint32_t k = (uint32_t)a.top_k;
+      bool topk_done = false;
+      if (!force_radix) {
+        // bound: the chunk maxima in bins <= btau number >= k, so >= k scores lie within chi of the max
+        for (int i = lane * 4; i < WNB; i += 128) *(uint4*)(hc + i) = make_uint4(0u, 0u, 0u, 0u);
+        __syncwarp();
+#pragma unroll
+        for (int s = 0; s < NS; ++s)
+          if (cm[s] > NEG) atomicAdd(hc + wbin(gmax, cm[s]), 1u);
+        __syncwarp();
+        u64 ab, wb;
+        const int btau = warp_crossing(hc, (u64)(k - 1), lane, ab, wb);
+        if (btau >= 0 && btau < WNB - 1) {  // the overflow bin bounds nothing
+          const float chi = (float)(btau + 1) * (1.0f / WBIN_SCALE);
+          uint32_t qual = 0;
+#pragma unroll
+          for (int s = 0; s < NS; ++s) qual |= (uint32_t)(cm[s] > NEG && wbin(gmax, cm[s]) <= btau) << s;
+          // each lane lists its qualifying chunks, one per round
+          int total = 0;
+          while (__any_sync(FULL, qual != 0u)) {
+            uint32_t cmask = 0;
+            float v[8];
+            int id0 = 0;
+            if (qual) {
+              const int s = __ffs(qual) - 1;
+              qual &= qual - 1u;
+              const int c = s * 32 + lane;
+              id0 = c * 8;
+              const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+              v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+              v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) cmask |= (uint32_t)(__fsub_rn(gmax, v[e]) < chi) << e;
+            }
+            const uint32_t cntl = __popc(cmask);
+            const uint32_t incl = warp_incl_scan_u32(cntl, lane);
+            int slot = total + (int)(incl - cntl);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              if ((cmask >> e) & 1u) {
+                if (slot < WCAP) {
+                  lx[slot] = v[e];
+                  lid[slot] = id0 + e;
+                }
+                ++slot;
+              }
+            }
+            total += (int)__shfl_sync(FULL, incl, 31);
+          }
+          __syncwarp();
+          if (total <= WCAP) {
+            n = total;
+            // exact k-th value: fine histogram over the list, then the crossing bin
+            const float s2 = (float)WNB / chi;
+            auto fbin = [&](float x) -> int {
+              float z = __fmul_rn(__fsub_rn(gmax, x), s2);
+              z = fminf(z, (float)(WNB - 1));
+              return __float2int_rz(z);
+            };
+            for (int i = lane * 4; i < WNB; i += 128) *(uint4*)(hc + i) = make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+            for (int j = lane; j < n; j += 32) atomicAdd(hc + fbin(lx[j]), 1u);
+            __syncwarp();
+            u64 above2, w2;
+            const int b2 = max(warp_crossing(hc, (u64)(k - 1), lane, above2, w2), 0);  // n >= k
+            int m = 0;
+            for (int j0 = 0; j0 < n; j0 += 32) {
+              const int j = j0 + lane;
+              const bool in = j < n && fbin(lx[j]) == b2;
+              const unsigned bm = __ballot_sync(FULL, in);
+              const int pos = m + __popc(bm & ((1u << lane) - 1u));
+              if (in && pos < WMINI) mx[pos] = lx[j];
+              m += __popc(bm);
+            }
+            __syncwarp();
+            float my_tk = NEG;
+            bool found = false;
+            if (m <= WMINI) {
+              for (int j = lane; j < m; j += 32) {
+                const float xi = mx[j];
+                uint32_t gt = 0, ge = 0;
+                for (int jj = 0; jj < m; ++jj) {
+                  gt += mx[jj] > xi;
+                  ge += mx[jj] >= xi;
+                }
+                if (above2 + gt <= k - 1 && k - 1 < above2 + ge) {
+                  my_tk = xi;
+                  found = true;
+                }
+              }
+            } else {
+              for (int j = lane; j < n; j += 32) {
+                const float xi = lx[j];
+                uint32_t gt = 0, ge = 0;
+                for (int jj = 0; jj < n; ++jj) {
+                  gt += lx[jj] > xi;
+                  ge += lx[jj] >= xi;
+                }
+                if (gt <= k - 1 && k - 1 < ge) {
+                  my_tk = xi;
+                  found = true;
+                }
+              }
+            }
+            const unsigned bal3 = __ballot_sync(FULL, found);
+            tk = __shfl_sync(FULL, my_tk, max(__ffs(bal3) - 1, 0));
+            // keep the survivors (x >= tk) at the front of the list
+            float sx[WCAP / 32];
+            int32_t si[WCAP / 32];
+#pragma unroll
+            for (int t2 = 0; t2 < WCAP / 32; ++t2) {
+              const int j = lane + 32 * t2;
+              sx[t2] = j < n ? lx[j] : NEG;
+              si[t2] = j < n ? lid[j] : 0;
+            }
+            __syncwarp();
+            int base = 0;
+#pragma unroll
+            for (int t2 = 0; t2 < WCAP / 32; ++t2) {
+              const bool keepj = sx[t2] >= tk && sx[t2] > NEG;
+              const unsigned bm = __ballot_sync(FULL, keepj);
+              if (keepj) {
+                const int pos = base + __popc(bm & ((1u << lane) - 1u));
+                lx[pos] = sx[t2];
+                lid[pos] = si[t2];
+              }
+              base += __popc(bm);
+            }
+            __syncwarp();
+            n = base;
+            topk_done = true;
+          }
+        }
+      }
+      if (!topk_done) {
+        // exact k-th over the whole row: count, then radix select over X
+        uint32_t nf = 0;
+        for (int c = lane; c < nch; c += 32) {
+          const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+          nf += finite_val(f0.x) + finite_val(f0.y) + finite_val(f0.z) + finite_val(f0.w) + finite_val(f1.x) +
+                finite_val(f1.y) + finite_val(f1.z) + finite_val(f1.w);
+        }
+        nf = __reduce_add_sync(FULL, nf);
+        n = -1;
+        if (k < nf) {
+          status |= MTR_ROW_SLOW_PATH;
+          uint32_t prefix = 0, mask = 0;
+          u64 above = 0, wlast = 0;
+#pragma unroll 1
+          for (int shift = 24; shift >= 0; shift -= 8) {
+            for (int i = lane * 4; i < WNB; i += 128) *(uint4*)(hc + i) = make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+            for (int id = lane; id < V; id += 32) {
+              const float x = *xat(id);
+              if (finite_val(x)) {
+                const uint32_t key = fkey(x);
+                if ((key & mask) == prefix) atomicAdd(hc + (255 - (int)((key >> shift) & 255u)), 1u);
+              }
+            }
+            __syncwarp();
+            u64 ab;
+            const int b = max(warp_crossing(hc, (u64)(k - 1) - above, lane, ab, wlast), 0);  // k <= finite count
+            above += ab;
+            prefix |= (255u - (uint32_t)b) << shift;
+            mask |= 255u << shift;
+            __syncwarp();
+          }
+          tk = key2f(prefix);
+          const u64 nge = above + wlast;
+          if (nge <= (u64)WCAP && !force_radix) {
+            // list the survivors in id order
+            int base = 0;
+            for (int id0 = 0; id0 < V; id0 += 32) {
+              const int id = id0 + lane;
+              float x = NEG;
+              if (id < V) x = *xat(id);
+              const bool keepj = finite_val(x) && x >= tk;
+              const unsigned bm = __ballot_sync(FULL, keepj);
+              const int pos = base + __popc(bm & ((1u << lane) - 1u));
+              if (keepj && pos < WCAP) {
+                lx[pos] = x;
+                lid[pos] = id;
+              }
+              base += __popc(bm);
+            }
+            __syncwarp();
+            n = min(base, WCAP);
+          }
+        }
+      }
+    }
+    if (!need_x_late && n >= 0) issue_next();  // X is no longer read by this row
+
+    // ---------------------------------------------------------- top-p and the draw
+    if (need_mass && n >= 0) {
+      // on the survivor list
+      for (int j = lane; j < n; j += 32) lq[j] = expfx(__fsub_rn(lx[j], gmax));
+      __syncwarp();
+      u64 tot = 0;
+      for (int j = lane; j < n; j += 32) tot += lq[j];
+      tot = warp_sum_u64(tot);
+      qkept = tot;
+      // distance bins of the survivors (monotone in x): s3 spreads [0, d_max] over the bins
+      float dmax = 0.0f;
+      for (int j = lane; j < n; j += 32) dmax = fmaxf(dmax, __fsub_rn(gmax, lx[j]));
+      dmax = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(dmax)));  // non-negative: bits order as floats
+      const float s3 = dmax > 0.0f ? (float)(WNB - 1) / dmax : 0.0f;
+      auto dbin3 = [&](float x) -> int {
+        float z = __fmul_rn(__fsub_rn(gmax, x), s3);
+        z = fminf(z, (float)(WNB - 1));
+        return __float2int_rz(z);
+      };
+      if (dv.topp_on) {
+        const double P = __dmul_rn((double)a.top_p, (double)tot);
+        const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+        for (int i = lane * 2; i < WNB; i += 64) *(ulonglong2*)(hist + i) = make_ulonglong2(0ull, 0ull);
+        __syncwarp();
+        for (int j = lane; j < n; j += 32)
+          if (lq[j]) atomicAdd(hist + dbin3(lx[j]), (u64)lq[j]);
+        __syncwarp();
+        u64 above3, w3;
+        const int b3 = max(warp_crossing(hist, plim, lane, above3, w3), 0);  // plim < total
+        // canonical order (score desc, id asc) inside the crossing bin
+        int m = 0;
+        for (int j0 = 0; j0 < n; j0 += 32) {
+          const int j = j0 + lane;
+          const bool in = j < n && lq[j] != 0u && dbin3(lx[j]) == b3;
+          const unsigned bm = __ballot_sync(FULL, in);
+          const int pos = m + __popc(bm & ((1u << lane) - 1u));
+          if (in && pos < WMINI) {
+            mx[pos] = lx[j];
+            mi[pos] = lid[j];
+            mq[pos] = lq[j];
+          }
+          m += __popc(bm);
+        }
+        __syncwarp();
+        float my_x = 0.0f;
+        int32_t my_id = NO_ID;
+        u64 my_q = 0;
+        bool found = false;
+        if (m <= WMINI) {
+          for (int j = lane; j < m; j += 32) {
+            const float xj = mx[j];
+            const int32_t ij = mi[j];
+            u64 am = above3;
+            for (int jj = 0; jj < m; ++jj)
+              if (canon_before(mx[jj], mi[jj], xj, ij)) am += mq[jj];
+            if (am <= plim && am + mq[j] > plim) {
+              my_x = xj;
+              my_id = ij;
+              my_q = am + mq[j];
+              found = true;
+            }
+          }
+        } else {
+          for (int j = lane; j < n; j += 32) {
+            const float xj = lx[j];
+            const int32_t ij = lid[j];
+            if (!lq[j]) continue;
+            u64 am = 0;
+            for (int jj = 0; jj < n; ++jj)
+              if (canon_before(lx[jj], lid[jj], xj, ij)) am += lq[jj];
+            if (am <= plim && am + lq[j] > plim) {
+              my_x = xj;
+              my_id = ij;
+              my_q = am + lq[j];
+              found = true;
+            }
+          }
+        }
+        const unsigned bf = __ballot_sync(FULL, found);
+        const int src = max(__ffs(bf) - 1, 0);
+        cut_x = __shfl_sync(FULL, my_x, src);
+        cut_id = __shfl_sync(FULL, my_id, src);
+        qkept = __shfl_sync(FULL, my_q, src);
+        topp_cut = true;
+        bool tie = false;
+        for (int j = lane; j < n; j += 32) tie |= lx[j] == cut_x && lid[j] > cut_id;
+        if (__any_sync(FULL, tie)) status |= MTR_ROW_TIE_AT_CUT;
+        __syncwarp();
+      }
+      if (sel == MTR_SELECT_SAMPLE) {
+        // id-ordered mass of the kept entries: id histogram, then the crossing bin
+        const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
+        int ish = 0;
+        while ((VP >> ish) > WNB) ++ish;
+        for (int i = lane * 2; i < WNB; i += 64) *(ulonglong2*)(hist + i) = make_ulonglong2(0ull, 0ull);
+        __syncwarp();
+        auto kept = [&](int j) -> bool {
+          return lq[j] != 0u && (!topp_cut || lx[j] > cut_x || (lx[j] == cut_x && lid[j] <= cut_id));
+        };
+        for (int j = lane; j < n; j += 32)
+          if (kept(j)) atomicAdd(hist + (lid[j] >> ish), (u64)lq[j]);
+        __syncwarp();
+        u64 above4, w4;
+        const int b4 = max(warp_crossing(hist, R, lane, above4, w4), 0);  // R < qkept
+        int m = 0;
+        for (int j0 = 0; j0 < n; j0 += 32) {
+          const int j = j0 + lane;
+          const bool in = j < n && kept(j) && (lid[j] >> ish) == b4;
+          const unsigned bm = __ballot_sync(FULL, in);
+          const int pos = m + __popc(bm & ((1u << lane) - 1u));
+          if (in && pos < WMINI) {
+            mi[pos] = lid[j];
+            mq[pos] = lq[j];
+          }
+          m += __popc(bm);
+        }
+        __syncwarp();
+        int32_t my_tok = NO_ID;
+        if (m <= WMINI) {
+          for (int j = lane; j < m; j += 32) {
+            const int32_t ij = mi[j];
+            u64 cm2 = above4;
+            for (int jj = 0; jj < m; ++jj)
+              if (mi[jj] <= ij) cm2 += mq[jj];
+            if (cm2 > R && cm2 - mq[j] <= R) my_tok = ij;
+          }
+        } else {
+          for (int j = lane; j < n; j += 32) {
+            if (!kept(j)) continue;
+            const int32_t ij = lid[j];
+            u64 cm2 = 0;
+            for (int jj = 0; jj < n; ++jj)
+              if (kept(jj) && lid[jj] <= ij) cm2 += lq[jj];
+            if (cm2 > R && cm2 - lq[j] <= R) my_tok = ij;
+          }
+        }
+        token = __reduce_min_sync(FULL, my_tok);
+      }
+    } else if (need_mass) {
+      // dense path over the whole row (no usable survivor list)
+      status |= MTR_ROW_SLOW_PATH;
+      u64 tot = 0;
+      for (int id = lane; id < V; id += 32) {
+        const float x = *xat(id);
+        if (finite_val(x) && x >= tk) tot += expfx(__fsub_rn(x, gmax));
+      }
+      tot = warp_sum_u64(tot);
+      qkept = tot;
+      if (dv.topp_on) {
+        const double P = __dmul_rn((double)a.top_p, (double)tot);
+        const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+        uint32_t prefix = 0, mask = 0;
+        u64 above = 0, lastw = 0;
+#pragma unroll 1
+        for (int shift = 24; shift >= 0; shift -= 8) {
+          for (int i = lane * 2; i < WNB; i += 64) *(ulonglong2*)(hist + i) = make_ulonglong2(0ull, 0ull);
+          __syncwarp();
+          for (int id = lane; id < V; id += 32) {
+            const float x = *xat(id);
+            if (finite_val(x) && x >= tk) {
+              const uint32_t key = fkey(x);
+              if ((key & mask) == prefix) {
+                const uint32_t q = expfx(__fsub_rn(x, gmax));
+                if (q) atomicAdd(hist + (255 - (int)((key >> shift) & 255u)), (u64)q);
+              }
+            }
+          }
+          __syncwarp();
+          u64 ab;
+          const int b = max(warp_crossing(hist, plim - above, lane, ab, lastw), 0);  // plim < total
+          above += ab;
+          prefix |= (255u - (uint32_t)b) << shift;
+          mask |= 255u << shift;
+          __syncwarp();
+        }
+        const float vstar = key2f(prefix);
+        // the tie group at vstar shares one q
+        uint32_t cnt_v = 0;
+        for (int id = lane; id < V; id += 32) cnt_v += (*xat(id) == vstar);
+        const uint32_t lastc = max(__reduce_add_sync(FULL, cnt_v), 1u);
+        const u64 qv = max(lastw / (u64)lastc, 1ull);
+        u64 nkeep = (plim - above) / qv + 1ull;
+        if (nkeep > lastc) nkeep = lastc;
+        cut_x = vstar;
+        cut_id = NO_ID;
+        if (nkeep < lastc) {
+          // the nkeep-th smallest id of the tie group
+          int32_t lo_id = -1;
+          uint32_t seen = 0;
+          for (int id0 = 0; id0 < V && seen < nkeep; id0 += 32) {
+            const int id = id0 + lane;
+            const bool hit = id < V && *xat(id) == vstar;
+            const unsigned bm = __ballot_sync(FULL, hit);
+            const uint32_t cb = __popc(bm);
+            if (seen + cb >= nkeep) {
+              unsigned mm = bm;
+              for (uint32_t r = 1; r < nkeep - seen; ++r) mm &= mm - 1;
+              lo_id = id0 + __ffs(mm) - 1;
+            }
+            seen += cb;
+          }
+          cut_id = lo_id;
+          status |= MTR_ROW_TIE_AT_CUT;
+        }
+        qkept = above + nkeep * qv;
+        topp_cut = true;
+      }
+      if (sel == MTR_SELECT_SAMPLE) {
+        const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
+        u64 run = 0;
+        int32_t tok = -1;
+        for (int id0 = 0; id0 < V && tok < 0; id0 += 32) {
+          const int id = id0 + lane;
+          u64 q = 0;
+          if (id < V) {
+            const float x = *xat(id);
+            const bool kp = finite_val(x) && x >= tk && (!topp_cut || x > cut_x || (x == cut_x && id <= cut_id));
+            q = kp ? expfx(__fsub_rn(x, gmax)) : 0u;
+          }
+          const u64 in = warp_incl_scan_u64(q, lane);
+          const bool hit = q != 0 && run + in > R && run + in - q <= R;
+          const unsigned bm = __ballot_sync(FULL, hit);
+          if (bm) tok = id0 + __ffs(bm) - 1;
+          run += __shfl_sync(FULL, in, 31);
+        }
+        token = tok;
+      }
+    }
+    if (!clean && sel == MTR_SELECT_SAMPLE) token = (int32_t)a.pad_id;
+
+    // ---------------------------------------------------------- processed scores / log-probs
+    if (need_x_late) {
+      const bool filter_out = clean && sel != MTR_SELECT_ARGMAX;
+      double lse = 0.0;
+      if (want_lp && clean) {
+        if (!need_mass || sel == MTR_SELECT_ARGMAX) {
+          u64 s = 0;
+          for (int id = lane; id < V; id += 32) {
+            const float x = *xat(id);
+            s += finite_val(x) ? expfx(__fsub_rn(x, gmax)) : 0u;
+          }
+          qkept = warp_sum_u64(s);
+        }
+        lse = log((double)qkept) - 31.0 * 0.69314718055994530942;
+      }
+      float* srow = a.out_scores ? a.out_scores + row * a.out_scores_row_stride : nullptr;
+      float* lrow = want_lp ? a.out_logprobs + row * a.out_logprobs_row_stride : nullptr;
+      for (int i = lane * 4; i < V; i += 128) {
+        const float4 f = *(const float4*)xat(i);
+        const float v[4] = {f.x, f.y, f.z, f.w};
+        float so[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool kp =
+              !filter_out || (v[e] >= tk && (!topp_cut || v[e] > cut_x || (v[e] == cut_x && i + e <= cut_id)));
+          so[e] = kp ? v[e] : NEG;
+          lo[e] = !clean ? __int_as_float(0x7fc00000)
+                         : (finite_val(v[e]) && kp) ? (float)(((double)v[e] - (double)gmax) - lse) : NEG;
+        }
+        if (srow) {
+          if (dv.out_vec) {
+            __stcs((float4*)(srow + i), make_float4(so[0], so[1], so[2], so[3]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (i + e < V) srow[i + e] = so[e];
+          }
+        }
+        if (lrow) {
+          if (dv.lp_vec) {
+            __stcs((float4*)(lrow + i), make_float4(lo[0], lo[1], lo[2], lo[3]));
+          } else {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              if (i + e < V) lrow[i + e] = lo[e];
+          }
+        }
+      }
+    }
+    issue_next();
+    if (lane == 0) {
+      int32_t mm = mono;
+      if (sel != MTR_SELECT_NONE) {
+        int64_t fin = token;
+        if (a.unfinished) {
+          const uint8_t uf = a.unfinished[row];
+          if (!uf) fin = a.pad_id;
+          a.unfinished[row] = (uint8_t)(uf && !is_eos(a, fin));
+        }
+        if (a.flags & MTR_FLAG_MONO_UPDATE_FROM_SAMPLE) mm = mono_update(a, mm, fin);
+        if ((a.flags & MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE) && a.prev_token) a.prev_token[row] = (int32_t)fin;
+        if (a.out_ids) a.out_ids[row] = fin;
+      }
+      if (a.mono_mode != MTR_MONO_OFF && a.mono_state) a.mono_state[row] = mm;
+      if (a.out_status) a.out_status[row] = status;
+    }
+    if (nrow < a.num_rows) load_ahead(a, dv, nrow, lane, L, ah);
+    __syncwarp();  // this row's readers of the shared regions are done
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 struct Geo {
@@ -1725,10 +2863,15 @@ static int validate(const MtrSamplerArgs* a) {
   if (!a) return MTR_ERR_NULL_ARG;
   if (a->abi_version != MTR_ABI_VERSION || a->struct_size != sizeof(MtrSamplerArgs)) return MTR_ERR_ABI;
   const uint32_t known = MTR_FLAG_MONO_UPDATE_FROM_IDS | MTR_FLAG_MONO_UPDATE_FROM_SAMPLE |
-                         MTR_FLAG_GRAMMAR_PREV_FROM_IDS | MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE | MTR_FLAG_FORCE_RADIX;
+                         MTR_FLAG_GRAMMAR_PREV_FROM_IDS | MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE | MTR_FLAG_FORCE_RADIX |
+                         MTR_FLAG_KERNEL_ROW_CTA | MTR_FLAG_KERNEL_ROW_WARP;
   if (a->flags & ~known) return MTR_ERR_BAD_PARAM;
+  if ((a->flags & MTR_FLAG_KERNEL_ROW_CTA) && (a->flags & MTR_FLAG_KERNEL_ROW_WARP)) return MTR_ERR_BAD_PARAM;
   if (a->num_rows < 0) return MTR_ERR_BAD_SHAPE;
   if (a->vocab < 1 || a->vocab > MTR_MAX_VOCAB) return MTR_ERR_BAD_SHAPE;
+  if ((a->flags & MTR_FLAG_KERNEL_ROW_WARP) &&
+      (a->vocab > WV_MAX || (a->input_ids && a->ids_len - a->penalty_start > WMAX_PEN_IDS)))
+    return MTR_ERR_UNSUPPORTED;
   if (a->num_rows == 0) return MTR_OK;
   if (!a->logits) return MTR_ERR_NULL_ARG;
   if (a->logits_dtype != MTR_DTYPE_F32 && a->logits_dtype != MTR_DTYPE_BF16 && a->logits_dtype != MTR_DTYPE_F16)
@@ -1834,6 +2977,9 @@ static Derived derive(const MtrSamplerArgs& a) {
   while (((a.vocab - 1) >> d.id_shift) >= NB) ++d.id_shift;
   d.gwords = (a.vocab + 31) / 32;
   d.temp_rcp = 1.0f / a.temperature;
+  d.neg_one = -1.0f;
+  d.neg_zero = -0.0f;
+  d.one = 1.0f;
   for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c)
     d.cond_rcp[c] = (c < a.n_cond && a.cond_temperature[c] > 0.0f) ? 1.0f / a.cond_temperature[c] : 1.0f;
   for (int r = 0; r < MTR_MAX_COL_TEMP_RANGES; ++r)
@@ -1871,6 +3017,51 @@ static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, 
     cfg.numAttrs = 1;
   }
   return cudaLaunchKernelEx(&cfg, kern, a, d);
+}
+
+// Kernel choice.  The row-per-warp kernel wins when many rows of a small
+// vocabulary each end in a short list (argmax, or top-k with k <= WARP_TOPK_MAX):
+// ~10 rows stay resident per SM with no block barrier.  Everything else (few
+// rows, large vocabularies, top-p over the whole row) takes the row-per-CTA
+// kernel.  The flags force either kernel.
+constexpr int WARP_TOPK_MAX = 128;
+enum { KERNEL_ROW_CTA = 0, KERNEL_ROW_WARP = 1 };
+static int pick_kernel(const MtrSamplerArgs& a, const Derived& d, int sms) {
+  if (a.flags & MTR_FLAG_KERNEL_ROW_CTA) return KERNEL_ROW_CTA;
+  if (a.flags & MTR_FLAG_KERNEL_ROW_WARP) return KERNEL_ROW_WARP;
+  if (a.vocab > WV_MAX || a.num_rows < 2 * (int64_t)sms) return KERNEL_ROW_CTA;
+  if (d.pen_on && a.ids_len - a.penalty_start > WMAX_PEN_IDS) return KERNEL_ROW_CTA;
+  const bool short_list = a.select_mode == MTR_SELECT_ARGMAX || (d.topk_on && a.top_k <= WARP_TOPK_MAX);
+  return short_list ? KERNEL_ROW_WARP : KERNEL_ROW_CTA;
+}
+
+// Persistent grid: as many one-warp CTAs as fit on the device (each walks rows
+// r, r + grid, ... and prefetches its next row into L2), at most one per row.
+template <typename Tin, bool CFG>
+static cudaError_t launch_warp_t(const MtrSamplerArgs& a, const Derived& d, cudaStream_t s) {
+  auto kern = row_warp_kernel<Tin, CFG>;
+  const int dyn = warp_bytes(a.vocab);
+  static int occ_cache[64] = {0}, occ_dyn[64] = {0};  // per instantiation and device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  int occ = occ_dyn[dev] == dyn ? occ_cache[dev] : 0;
+  if (occ == 0) {
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, 32, (size_t)dyn);
+    if (e != cudaSuccess) return e;
+    if (occ < 1) occ = 1;
+    occ_cache[dev] = occ;
+    occ_dyn[dev] = dyn;
+  }
+  const int64_t cap = (int64_t)occ * device_sms();
+  const unsigned grid = (unsigned)(a.num_rows < cap ? a.num_rows : cap);
+  kern<<<grid, 32, (size_t)dyn, s>>>(a, d);
+  return cudaGetLastError();
+}
+template <typename Tin>
+static cudaError_t launch_warp(const MtrSamplerArgs& a, const Derived& d, cudaStream_t s) {
+  return a.cfg_enabled ? launch_warp_t<Tin, true>(a, d, s) : launch_warp_t<Tin, false>(a, d, s);
 }
 
 template <typename Tin>
@@ -1924,7 +3115,39 @@ int mtr_sampler_query(int32_t vocab, int32_t num_rows, int32_t with_penalties, M
   out->max_vocab = MTR_MAX_VOCAB;
   out->max_ids_len = MTR_MAX_IDS_LEN;
   out->candidate_cap = mtr::CAP;
+  out->kernel = mtr::KERNEL_ROW_CTA;
   return MTR_OK;
+}
+
+int mtr_sampler_query_args(const MtrSamplerArgs* a, MtrLaunchInfo* out) {
+  if (!out) return MTR_ERR_NULL_ARG;
+  const int v = mtr::validate(a);
+  if (v != MTR_OK) return v;
+  const mtr::Derived d = mtr::derive(*a);
+  const int sms = mtr::device_sms();
+  if (mtr::pick_kernel(*a, d, sms) == mtr::KERNEL_ROW_WARP) {
+    out->threads = 32;
+    out->elems_per_thread = mtr::warp_vpad(a->vocab) / 32;
+    out->cluster_size = 1;
+    int occ = 0;
+    const int dyn = mtr::warp_bytes(a->vocab);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, mtr::row_warp_kernel<__nv_bfloat16, true>, 32, (size_t)dyn) !=
+            cudaSuccess ||
+        occ < 1) {
+      cudaGetLastError();
+      occ = 9;  // no device: the launch bound
+    }
+    const int64_t cap = (int64_t)occ * sms;
+    out->grid = (int32_t)(a->num_rows < cap ? a->num_rows : cap);
+    out->dyn_smem_bytes = mtr::warp_bytes(a->vocab);
+    out->max_vocab = MTR_MAX_VOCAB;
+    out->max_ids_len = MTR_MAX_IDS_LEN;
+    out->candidate_cap = mtr::WCAP;
+    out->kernel = mtr::KERNEL_ROW_WARP;
+    return MTR_OK;
+  }
+  const int rc = mtr_sampler_query(a->vocab, a->num_rows, d.pen_on, out);
+  return rc;
 }
 
 int mtr_sampler_launch(const MtrSamplerArgs* a, void* stream) {
@@ -1932,10 +3155,20 @@ int mtr_sampler_launch(const MtrSamplerArgs* a, void* stream) {
   if (v != MTR_OK) return v;
   if (a->num_rows == 0) return MTR_OK;
   const mtr::Derived d = mtr::derive(*a);
-  const mtr::Geo g = mtr::pick_geo(a->vocab, a->num_rows, mtr::device_sms());
-  const int dyn = mtr::dyn_smem_bytes(g, d.pen_on != 0);
+  const int sms = mtr::device_sms();
   cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
+  if (mtr::pick_kernel(*a, d, sms) == mtr::KERNEL_ROW_WARP) {
+    switch (a->logits_dtype) {
+      case MTR_DTYPE_F32: e = mtr::launch_warp<float>(*a, d, s); break;
+      case MTR_DTYPE_BF16: e = mtr::launch_warp<__nv_bfloat16>(*a, d, s); break;
+      default: e = mtr::launch_warp<__half>(*a, d, s); break;
+    }
+    mtr::g_last_cuda_error = (int)e;
+    return e == cudaSuccess ? MTR_OK : MTR_ERR_CUDA;
+  }
+  const mtr::Geo g = mtr::pick_geo(a->vocab, a->num_rows, sms);
+  const int dyn = mtr::dyn_smem_bytes(g, d.pen_on != 0);
   switch (a->logits_dtype) {
     case MTR_DTYPE_F32: e = mtr::launch_dtype<float>(*a, d, g, dyn, s); break;
     case MTR_DTYPE_BF16: e = mtr::launch_dtype<__nv_bfloat16>(*a, d, g, dyn, s); break;

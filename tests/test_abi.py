@@ -142,6 +142,42 @@ def test_query_geometry(lib, vocab, rows, cs):
     assert info.dyn_smem_bytes == info.threads * info.elems_per_thread * 10
 
 
+@pytest.mark.parametrize("rows,vocab,top_k,select,flags,kernel", [
+    (4096, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_WARP),      # many rows, short top-k list
+    (4096, 4096, 0, N.SELECT_ARGMAX, 0, N.KERNEL_ROW_WARP),
+    (64, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),         # few rows: latency geometry
+    (4096, 4096, 0, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),        # top-p over the whole row
+    (4096, 4096, 500, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),      # long top-k list
+    (4096, 8192, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),       # vocabulary above 4096
+    (4096, 4096, 50, N.SELECT_SAMPLE, N.FLAG_KERNEL_ROW_CTA, N.KERNEL_ROW_CTA),
+    (8, 4096, 0, N.SELECT_SAMPLE, N.FLAG_KERNEL_ROW_WARP, N.KERNEL_ROW_WARP),
+])
+def test_query_args_kernel_choice(lib, rows, vocab, top_k, select, flags, kernel):
+    a = _valid_args()
+    a.num_rows, a.vocab, a.logits_row_stride = rows, vocab, vocab
+    a.top_k, a.select_mode, a.flags = top_k, select, flags
+    info = N.query_args(a)
+    assert info.kernel == kernel
+    if kernel == N.KERNEL_ROW_WARP:
+        assert (info.threads, info.cluster_size) == (32, 1)
+        assert min(rows, 148) <= info.grid <= rows  # persistent: at most one warp per row
+        assert info.threads * info.elems_per_thread >= vocab
+        assert info.dyn_smem_bytes <= 48 * 1024
+    else:
+        assert info.grid == rows * info.cluster_size
+
+
+def test_kernel_flags_validated(lib):
+    a = _valid_args()
+    a.flags = N.FLAG_KERNEL_ROW_CTA | N.FLAG_KERNEL_ROW_WARP
+    assert N.validate(a) == N.ERR_BAD_PARAM
+    a.flags = N.FLAG_KERNEL_ROW_WARP
+    a.vocab = a.logits_row_stride = 4097
+    assert N.validate(a) == N.ERR_UNSUPPORTED
+    a.vocab = a.logits_row_stride = 4096
+    assert N.validate(a) == N.OK
+
+
 def test_status_strings(lib):
     assert N.status_string(N.OK) == "MTR_OK"
     assert N.status_string(N.ERR_ABI) == "MTR_ERR_ABI"

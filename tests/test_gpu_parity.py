@@ -12,10 +12,30 @@ from tests import _golden as G
 
 pytestmark = pytest.mark.gpu
 
+_KERNEL_FLAGS = {"cta": N.FLAG_KERNEL_ROW_CTA, "warp": N.FLAG_KERNEL_ROW_WARP}
+_kernel = {"name": "cta"}
+
+
+@pytest.fixture(autouse=True, params=["cta", "warp"])
+def kernel(request):
+    """Every parity case runs on both kernels (the row-per-warp kernel takes
+    vocabularies up to 4096 only)."""
+    _kernel["name"] = request.param
+    yield request.param
+    _kernel["name"] = "cta"
+
+
+def forced(s):
+    """`s` with the current kernel forced; skips vocabularies the kernel does not take."""
+    if _kernel["name"] == "warp" and s.vocab > 4096:
+        pytest.skip("row-per-warp kernel: vocab <= 4096")
+    return s.with_(flags=(s.flags & ~(N.FLAG_KERNEL_ROW_CTA | N.FLAG_KERNEL_ROW_WARP)) | _KERNEL_FLAGS[_kernel["name"]])
+
 
 def run_both(s, device):
     import torch
 
+    s = forced(s)
     ref = oracle.run(s)
     dev = DeviceStep(s, device)
     dev.launch()
@@ -188,8 +208,8 @@ def test_finished_rows_and_eos(cuda_device):
 def test_state_carried_over_steps(cuda_device):
     import torch
 
-    base = W.batched_decode(seed=71, pairs=48).with_(
-        flags=N.FLAG_MONO_UPDATE_FROM_SAMPLE | N.FLAG_GRAMMAR_UPDATE_FROM_SAMPLE, sos_ids=(4094, 3000))
+    base = forced(W.batched_decode(seed=71, pairs=48).with_(
+        flags=N.FLAG_MONO_UPDATE_FROM_SAMPLE | N.FLAG_GRAMMAR_UPDATE_FROM_SAMPLE, sos_ids=(4094, 3000)))
     rng = np.random.default_rng(72)
     host = base
     dev = None
@@ -223,7 +243,7 @@ def test_scan_equals_incremental_state(cuda_device):
             inc = scan.with_(mono_state=np.full(B, -1, np.int32))
         else:
             inc = scan.with_(mono_mode=N.MONO_STATE, flags=N.FLAG_MONO_UPDATE_FROM_IDS, mono_state=state)
-        dev = DeviceStep(inc, cuda_device)
+        dev = DeviceStep(forced(inc), cuda_device)
         dev.launch()
         torch.cuda.synchronize()
         got = dev.results()
@@ -237,7 +257,7 @@ def test_reference_fixture_processed_scores(cuda_device, name):
     import torch
 
     c = G.case(name)
-    dev = DeviceStep(G.chain_step(name), cuda_device)
+    dev = DeviceStep(forced(G.chain_step(name)), cuda_device)
     dev.launch()
     torch.cuda.synchronize()
     got = dev.results()["out_scores"]
@@ -251,7 +271,7 @@ def test_reference_fixture_processed_scores(cuda_device, name):
 def test_cuda_graph_capture_replay(cuda_device):
     import torch
 
-    s = W.penalty_sweep(seed=91, rows=256)
+    s = forced(W.penalty_sweep(seed=91, rows=256))
     dev = DeviceStep(s, cuda_device)
     stream = torch.cuda.Stream(cuda_device)
     dev.launch(stream)  # warm (sets kernel attributes outside capture)
