@@ -153,6 +153,11 @@ __device__ __forceinline__ void expfx2(float d0, float d1, uint32_t& q0, uint32_
 // x / t correctly rounded, given y = RN(1/t) (Markstein: q0 = x*y, r = x - q0*t
 // exactly, q = q0 + r*y).  Magnitudes outside [2^-60, 2^60) and NaN take the
 // IEEE divide; zeros and infinities pass through (t is positive and finite).
+// out of line: the rare operands keep the IEEE divide away from the hot code
+__device__ __noinline__ float div_rare(float x, float t) {
+  if (x == 0.0f || fabsf(x) == pos_inf()) return x;
+  return __fdiv_rn(x, t);
+}
 __device__ __forceinline__ float div_by(float x, float t, float y) {
   const float ax = fabsf(x);
   if (ax >= 0x1p-60f && ax < 0x1p60f) {
@@ -160,8 +165,7 @@ __device__ __forceinline__ float div_by(float x, float t, float y) {
     const float r = __fmaf_rn(-q0, t, x);
     return __fmaf_rn(r, y, q0);
   }
-  if (x == 0.0f || ax == pos_inf()) return x;
-  return __fdiv_rn(x, t);
+  return div_rare(x, t);
 }
 
 // the same on a pair; fma(q0, -t, x) is bit-identical to fma(-q0, t, x)
@@ -504,6 +508,7 @@ struct Derived {
   // -1, -0 and 1 as launch parameters: FMAs with them stay FMAs (a compile-time
   // constant would let the compiler turn them into a mul + add pair and fuse it)
   float neg_one, neg_zero, one;
+  float rep_rcp;  // RN(1 / repetition_penalty) when it lies in [2^-30, 2^30] (Markstein divide), else 0
 };
 
 // Push the elements of this thread whose bit is set in `mask` to the local
@@ -1781,6 +1786,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* m, uint32_t parity) {
 }
 // bounded wait for phase `parity`; false when the copy did not land in time
 __device__ __forceinline__ bool mbar_wait(uint64_t* m, uint32_t parity) {
+#pragma unroll 1
   for (uint32_t i = 0; i < WAIT_POLLS; ++i)
     if (mbar_try_wait(m, parity)) return true;
   return false;
@@ -1838,6 +1844,11 @@ __device__ __forceinline__ int warp_crossing(const W* h, u64 lim, int lane, u64&
   return __shfl_sync(FULL, my_b, src);
 }
 
+__device__ __noinline__ void div_chunk_rare(float (&v)[8], float t, float y) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = div_by(v[e], t, y);
+}
+
 // x / t for a chunk (y = RN(1/t)): Markstein on pairs when every value that is
 // not -inf lies in [2^-60, 2^60) (-inf passes through), the IEEE divide per
 // element otherwise.
@@ -1859,8 +1870,21 @@ __device__ __forceinline__ void div_chunk(float (&v)[8], float t, float y) {
       v[e + 1] = v[e + 1] == neg_inf() ? v[e + 1] : q1;
     }
   } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = div_by(v[e], t, y);
+    div_chunk_rare(v, t, y);
+  }
+}
+
+// a chunk that a column-range edge splits: element by element (out of line)
+__device__ __noinline__ void temp_chunk_split(const MtrSamplerArgs& a, const Derived& dv, float (&v)[8], int id0) {
+  for (int e = 0; e < 8; ++e) {
+    float te = a.temperature, ye = dv.temp_rcp;
+#pragma unroll 1
+    for (int r = a.n_col_ranges - 1; r >= 0; --r)
+      if (id0 + e >= a.col_start[r] && id0 + e < a.col_end[r]) {
+        te = a.col_temperature[r];
+        ye = dv.col_rcp[r];
+      }
+    if (te != 1.0f) v[e] = div_by(v[e], te, ye);
   }
 }
 
@@ -1874,6 +1898,7 @@ __device__ __forceinline__ void temp_chunk(const MtrSamplerArgs& a, const Derive
   }
   float t0 = a.temperature, y0 = dv.temp_rcp, t1 = a.temperature;
   bool uniform_chunk = true;
+#pragma unroll 1
   for (int r = a.n_col_ranges - 1; r >= 0; --r) {
     const int cs = a.col_start[r], ce = a.col_end[r];
     if (id0 >= cs && id0 < ce) {
@@ -1887,28 +1912,54 @@ __device__ __forceinline__ void temp_chunk(const MtrSamplerArgs& a, const Derive
     if (t0 != 1.0f) div_chunk(v, t0, y0);
     return;
   }
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    float te = a.temperature, ye = dv.temp_rcp;
-    for (int r = a.n_col_ranges - 1; r >= 0; --r)
-      if (id0 + e >= a.col_start[r] && id0 + e < a.col_end[r]) {
-        te = a.col_temperature[r];
-        ye = dv.col_rcp[r];
-      }
-    if (te != 1.0f) v[e] = div_by(v[e], te, ye);
-  }
+  temp_chunk_split(a, dv, v, id0);
 }
 
-// per-row values loaded one row ahead (independent loads only)
-struct WarpAhead {
-  int32_t hid[WHIST];  // ids at positions hbase + lane + 32k (INT32_MIN: outside int32)
-  int32_t hbase;
-  int64_t s0;          // lane 0: mono_state; lane 1: previous token; lane 2/3 unused
-  int64_t s1;          // lane 0: last id (mono update); lane 3: uniform bits
-  int64_t cond[MTR_MAX_COND_TEMPS];  // lane 2: ids at L - cond_offset[c]
-};
+// Warp bitonic sort of 32*E distinct (or zero) u64 keys, descending; lane l
+// holds positions l*E .. l*E+E-1.
 
-__device__ __forceinline__ int32_t narrow_id(int64_t t) {
+// Bitonic sort of 64 u64 keys held two per lane (positions 2*lane, 2*lane+1), descending.
+__device__ __forceinline__ void sort64_desc(u64& a0, u64& a1, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j >= 2; j >>= 1) {
+      const u64 p0 = __shfl_xor_sync(FULL, a0, j >> 1), p1 = __shfl_xor_sync(FULL, a1, j >> 1);
+      const int g = 2 * lane;  // both positions share the bits k and j
+      const bool keep_larger = ((g & k) == 0) == ((g & j) == 0);
+      a0 = keep_larger ? (p0 > a0 ? p0 : a0) : (p0 < a0 ? p0 : a0);
+      a1 = keep_larger ? (p1 > a1 ? p1 : a1) : (p1 < a1 ? p1 : a1);
+    }
+    const bool desc = ((2 * lane) & k) == 0;
+    const bool sw = desc ? a0 < a1 : a0 > a1;
+    const u64 t0 = sw ? a1 : a0, t1 = sw ? a0 : a1;
+    a0 = t0;
+    a1 = t1;
+  }
+}
+// per-row values loaded one row ahead.  Loads only: every value stays raw
+// (no arithmetic on a loaded register) until the row that uses it, so issuing
+// them never waits on memory.
+struct WarpAhead {
+  u64 hid[WHIST];  // raw ids at positions hbase + lane + 32k (int32 ids zero-extended)
+  int32_t hbase;
+  u64 s0;          // lane 0: mono_state; lane 1: previous token (raw)
+  u64 s1;          // lane 0: last id (mono update); lane 3: uniform bits
+  u64 cond[MTR_MAX_COND_TEMPS];  // lane 2: raw ids at L - cond_offset[c]
+};
+constexpr u64 RAW_NONE = 0x8000000000000000ull;  // an id that lies outside int32: never valid
+
+__device__ __forceinline__ u64 load_raw_id(const MtrSamplerArgs& a, int64_t row, int64_t pos) {
+  const int64_t off = row * a.ids_row_stride + pos;
+  if (a.ids_dtype == MTR_IDS_I32) return (u64)__ldg((const uint32_t*)a.input_ids + off);
+  return (u64)__ldg((const unsigned long long*)a.input_ids + off);
+}
+__device__ __forceinline__ int64_t raw_id(const MtrSamplerArgs& a, u64 raw) {
+  return a.ids_dtype == MTR_IDS_I32 ? (int64_t)(int32_t)(uint32_t)raw : (int64_t)raw;
+}
+// as int32 (INT32_MIN when the id does not fit)
+__device__ __forceinline__ int32_t narrow_raw(const MtrSamplerArgs& a, u64 raw) {
+  const int64_t t = raw_id(a, raw);
   return (t >= INT32_MIN && t <= INT32_MAX) ? (int32_t)t : INT32_MIN;
 }
 
@@ -1919,28 +1970,32 @@ __device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derive
 #pragma unroll
   for (int k = 0; k < WHIST; ++k) {
     const int pos = w.hbase + lane + 32 * k;
-    w.hid[k] = (need_hist && pos < L) ? narrow_id(load_id(a, row, pos)) : INT32_MIN;
+    w.hid[k] = RAW_NONE;
+    if (need_hist && pos < L) w.hid[k] = load_raw_id(a, row, pos);
   }
   w.s0 = 0;
   w.s1 = 0;
   if (lane == 0) {
-    if (a.mono_mode == MTR_MONO_STATE) w.s0 = a.mono_state[row];
-    if (L > 0 && (a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS)) w.s1 = load_id(a, row, L - 1);
+    if (a.mono_mode == MTR_MONO_STATE) w.s0 = (u64)(uint32_t)a.mono_state[row];
+    if (L > 0 && (a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS)) w.s1 = load_raw_id(a, row, L - 1);
   } else if (lane == 1) {
-    w.s0 = -1;
+    w.s0 = RAW_NONE;
     if (a.grammar_class_of) {
-      if (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) w.s0 = L > 0 ? load_id(a, row, L - 1) : -1;
-      else if (a.prev_token) w.s0 = a.prev_token[row];
+      if (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) {
+        if (L > 0) w.s0 = load_raw_id(a, row, L - 1);
+      } else if (a.prev_token) {
+        w.s0 = (u64)(uint32_t)a.prev_token[row];
+      }
     }
   } else if (lane == 3) {
-    if (a.select_mode == MTR_SELECT_SAMPLE) w.s1 = (int64_t)__float_as_uint(a.uniforms[row]);
+    if (a.select_mode == MTR_SELECT_SAMPLE) w.s1 = (u64)__float_as_uint(a.uniforms[row]);
   }
 #pragma unroll
   for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c) {
-    w.cond[c] = -1;
+    w.cond[c] = RAW_NONE;
     if (lane == 2 && a.temp_mode == MTR_TEMP_ROW_CONDITIONAL && c < a.n_cond) {
       const int off = a.cond_offset[c];
-      if (off >= 1 && L >= off) w.cond[c] = load_id(a, row, L - off);
+      if (off >= 1 && L >= off) w.cond[c] = load_raw_id(a, row, L - off);
     }
   }
 }
@@ -2004,8 +2059,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
   for (; row < a.num_rows; row += gridDim.x) {
     const int64_t nrow = row + gridDim.x;
     bool issued = false;
-    auto issue_next = [&]() {
-      if (issued) return;
+    auto issue_next = [&]() {  // the next row's copy (its per-row values follow at the call site)
       issued = true;
       fence_proxy_async();
       __syncwarp();
@@ -2028,10 +2082,12 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       u64 gb = 0;
       float t = a.temperature, y = dv.temp_rcp, uu = 0.0f;
       if (lane == 0 && a.mono_mode == MTR_MONO_STATE) {
-        m0 = (int32_t)ah.s0;
-        if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) m0 = mono_update(a, m0, ah.s1);
+        m0 = (int32_t)(uint32_t)ah.s0;
+        if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) m0 = mono_update(a, m0, raw_id(a, ah.s1));
       } else if (lane == 1 && a.grammar_class_of) {
-        const int64_t prev = ah.s0;
+        const int64_t prev = ah.s0 == RAW_NONE ? -1
+                             : ((a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) ? raw_id(a, ah.s0)
+                                                                          : (int64_t)(int32_t)(uint32_t)ah.s0);
         if (prev >= V) st |= MTR_ROW_BAD_ID;
         if (prev >= 0 && prev < V) {
           const uint32_t c = __ldg(a.grammar_class_of + prev);
@@ -2044,12 +2100,15 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           }
         }
       } else if (lane == 2 && a.temp_mode == MTR_TEMP_ROW_CONDITIONAL) {
-        for (int c = 0; c < a.n_cond; ++c) {
-          const int64_t tok = ah.cond[c];
-          if (tok >= 0 && tok < V && ((__ldg(a.cond_token_bits[c] + (tok >> 5)) >> (tok & 31)) & 1u)) {
+        bool hit = false;  // first matching condition wins (static indices keep ah in registers)
+#pragma unroll
+        for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c) {
+          const int64_t tok = ah.cond[c] == RAW_NONE ? -1 : raw_id(a, ah.cond[c]);
+          if (!hit && c < a.n_cond && tok >= 0 && tok < V &&
+              ((__ldg(a.cond_token_bits[c] + (tok >> 5)) >> (tok & 31)) & 1u)) {
             t = a.cond_temperature[c];
             y = dv.cond_rcp[c];
-            break;
+            hit = true;
           }
         }
       } else if (lane == 3 && sel == MTR_SELECT_SAMPLE) {
@@ -2078,7 +2137,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
 #pragma unroll
       for (int k = 0; k < WHIST; ++k) {
         const int pos = ah.hbase + lane + 32 * k;
-        const int32_t t = ah.hid[k];
+        const int32_t t = narrow_raw(a, ah.hid[k]);
         if (pos < L && t != INT32_MIN) {
           if (t >= a.ts_start && t < a.ts_end) {
             lts = pos;
@@ -2087,6 +2146,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           if (is_sos(a, t)) lsos = pos;
         }
       }
+#pragma unroll 1
       for (int base = ah.hbase - 32; base > -32 && __all_sync(FULL, lts < 0 && lsos < 0); base -= 32) {
         // neither seen in the register window: walk back (long histories only)
         const int pos = base + lane;
@@ -2113,21 +2173,49 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
     }
     const int mono_hi = mono >= 0 ? (int32_t)min((int64_t)a.ts_end, (int64_t)a.ts_start + mono) : -1;
     const bool masks = mono_hi > a.ts_start || gon || (V & 7) != 0;
+    // grammar bitmap words of this lane's 16 chunks: issued now, used after the counts
+    uint32_t gw[NS];
+#pragma unroll
+    for (int s = 0; s < NS; ++s) {
+      const int id0 = (s * 32 + lane) * 8;
+      gw[s] = 0xffffffffu;
+      if (gon && gbits && id0 < V) gw[s] = __ldg(gbits + (id0 >> 5));
+    }
 
     // ---------------------------------------------------------- history counts
+    uint32_t own = 0;  // bit k: this lane counted window id k first and applies its penalties
+    const bool long_hist = a.penalty_start < ah.hbase;  // ids outside the register window
+    int32_t ht[WHIST];  // window ids inside the penalty window and [0, V), else -1
     if (dv.pen_on) {
-      for (int i = lane * 4; i < VP / 2; i += 128) *(uint4*)(cnt + i) = make_uint4(0u, 0u, 0u, 0u);
-      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < WV_MAX / 256; ++i) {
+        const int w = (i * 32 + lane) * 4;
+        if (w < VP / 2) *(uint4*)(cnt + w) = make_uint4(0u, 0u, 0u, 0u);
+      }
       uint32_t bad = 0;
 #pragma unroll
       for (int k = 0; k < WHIST; ++k) {
         const int pos = ah.hbase + lane + 32 * k;
-        const int32_t t = ah.hid[k];
-        if (pos >= a.penalty_start && pos < L) {
-          if (t < 0 || t >= V) bad = 1;
-          else atomicAdd(cnt + (t >> 1), 1u << (16 * (t & 1)));
-        }
+        const int32_t t = narrow_raw(a, ah.hid[k]);
+        const bool in_window = pos >= a.penalty_start && pos < L;
+        const bool ok = in_window && t >= 0 && t < V;
+        bad |= (uint32_t)(in_window && !ok);
+        ht[k] = ok ? t : -1;
       }
+      __syncwarp();
+#pragma unroll
+      for (int h0 = 0; h0 < WHIST; h0 += WHIST / 2) {
+        uint32_t old[WHIST / 2];  // a half window of atomics in flight before any result is used
+#pragma unroll
+        for (int k = 0; k < WHIST / 2; ++k) {
+          old[k] = 0xffffffffu;
+          if (ht[h0 + k] >= 0) old[k] = atomicAdd(cnt + (ht[h0 + k] >> 1), 1u << (16 * (ht[h0 + k] & 1)));
+        }
+#pragma unroll
+        for (int k = 0; k < WHIST / 2; ++k)
+          own |= (uint32_t)(ht[h0 + k] >= 0 && ((old[k] >> (16 * (ht[h0 + k] & 1))) & 0xffffu) == 0u) << (h0 + k);
+      }
+#pragma unroll 1
       for (int pos = a.penalty_start + lane; pos < ah.hbase; pos += 32) {  // long histories only
         const int64_t t = load_id(a, row, pos);
         if (t < 0 || t >= V) bad = 1;
@@ -2135,6 +2223,36 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       }
       if (__any_sync(FULL, bad)) status |= MTR_ROW_BAD_ID;
       __syncwarp();
+    }
+
+    // keep bits of this lane's 16 chunks: slot s in bits 8s .. 8s+7 of km[s >> 3]
+    u64 km[2] = {~0ull, ~0ull};
+    if (masks) {
+#pragma unroll
+      for (int s = 0; s < NS; ++s) {
+        const int id0 = (s * 32 + lane) * 8;
+        uint32_t keep = 0;
+        if (id0 < V) {
+          keep = range_bits(0, V - id0) & ~range_bits(a.ts_start - id0, mono_hi - id0);
+          if (gon) {
+            if (gbits) {
+              keep &= gw[s] >> (id0 & 31);
+            } else {
+              uint32_t g = 0;
+              const uint32_t ncls = (uint32_t)a.grammar_n_classes;
+#pragma unroll 1
+              for (int e = 0; e < 8; ++e) {
+                if (id0 + e < V) {
+                  const uint32_t cl = __ldg(a.grammar_class_of + id0 + e);
+                  g |= (cl < ncls ? (allow >> cl) & 1u : 0u) << e;
+                }
+              }
+              keep &= g;
+            }
+          }
+        }
+        km[s >> 3] = (km[s >> 3] & ~(0xffull << (8 * (s & 7)))) | ((u64)(keep & 0xffu) << (8 * (s & 7)));
+      }
     }
 
     // ---------------------------------------------------------- this row's logits
@@ -2153,97 +2271,163 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
     // Masks only ever write -inf, which bias, penalties and temperature map to
     // -inf again, so the order here (masks before or after temperature)
     // reproduces CFG -> masks -> bias -> penalties -> temperature exactly.
-#pragma unroll 1
-    for (int s = 0; s < NS; ++s) {
-      const int c = s * 32 + lane;
-      const int id0 = c * 8;
-      if (id0 >= V) break;
-      uint4 ra[NV];
+    // The common case (16-bit rows staged in place, no bias, no temperature in
+    // this pass) runs a loop with every launch-uniform test hoisted out of it.
+    bool fast_pass = false;
+    if constexpr (SPLIT) {
+      fast_pass = bulk && a.timeshift_bias == 0.0f &&
+                  (dv.pen_on || (a.temp_mode == MTR_TEMP_SCALAR && t_row == 1.0f));
+    }
+    if (fast_pass) {
+      if constexpr (SPLIT) {
+        float* const Xlo = X + 4 * lane;
+        float* const Xhi = X + HALF + 4 * lane;
+#pragma unroll 2
+        for (int s = 0; s < NS; ++s) {
+          if ((s * 32 + lane) * 8 >= V) break;
+          const uint4 ra = *(const uint4*)(Xlo + 128 * s);
+          float v[8];
+          if constexpr (CFG) {
+            const uint4 rb = *(const uint4*)(Xhi + 128 * s);
 #pragma unroll
-      for (int h = 0; h < NV; ++h) {
-        if (bulk) ra[h] = *(const uint4*)(lo_of(c) + 4 * h);
-        else ra[h] = E::gather(r1, id0 + h * VEC, V);
+            for (int e = 0; e < 8; e += 2) {
+              const u64 A = pk2(E::get(ra, e), E::get(ra, e + 1));
+              const u64 B = pk2(E::get(rb, e), E::get(rb, e + 1));
+              up2(fma2(fma2(fma2(B, NEG1, A), SC, NZ), ONE, B), v[e], v[e + 1]);
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = E::get(ra, e);
+          }
+          if (masks) {
+            const uint32_t keep = (uint32_t)((s < 8 ? km[0] : km[1]) >> (8 * (s & 7)));
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = ((keep >> e) & 1u) ? v[e] : NEG;
+          }
+          *(float4*)(Xlo + 128 * s) = make_float4(v[0], v[1], v[2], v[3]);
+          *(float4*)(Xhi + 128 * s) = make_float4(v[4], v[5], v[6], v[7]);
+        }
       }
-      float v[8];
-      if constexpr (CFG) {
-        uint4 rb[NV];
+    } else {
+#pragma unroll 1
+      for (int s = 0; s < NS; ++s) {
+        const int c = s * 32 + lane;
+        const int id0 = c * 8;
+        if (id0 >= V) continue;
+        uint4 ra[NV];
 #pragma unroll
         for (int h = 0; h < NV; ++h) {
-          if (SPLIT && bulk) rb[h] = *(const uint4*)(hi_of(c) + 4 * h);
-          else if (bulk) rb[h] = __ldcs((const uint4*)(r2 + id0 + h * VEC));
-          else rb[h] = E::gather(r2, id0 + h * VEC, V);
+          if (bulk) ra[h] = *(const uint4*)(lo_of(c) + 4 * h);
+          else ra[h] = E::gather(r1, id0 + h * VEC, V);
         }
-        // b + (a - b) * s as three FMAs whose -1 / -0 / 1 operands are launch
-        // parameters, so the compiler cannot form a fusable mul + add pair
+        float v[8];
+        if constexpr (CFG) {
+          uint4 rb[NV];
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const u64 A = pk2(E::get(ra[e / VEC], e % VEC), E::get(ra[e / VEC], e % VEC + 1));
-          const u64 B = pk2(E::get(rb[e / VEC], e % VEC), E::get(rb[e / VEC], e % VEC + 1));
-          up2(fma2(fma2(fma2(B, NEG1, A), SC, NZ), ONE, B), v[e], v[e + 1]);
+          for (int h = 0; h < NV; ++h) {
+            if (SPLIT && bulk) rb[h] = *(const uint4*)(hi_of(c) + 4 * h);
+            else if (bulk) rb[h] = __ldcs((const uint4*)(r2 + id0 + h * VEC));
+            else rb[h] = E::gather(r2, id0 + h * VEC, V);
+          }
+          // b + (a - b) * s as three FMAs whose -1 / -0 / 1 operands are launch
+          // parameters, so the compiler cannot form a fusable mul + add pair
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) {
+            const u64 A = pk2(E::get(ra[e / VEC], e % VEC), E::get(ra[e / VEC], e % VEC + 1));
+            const u64 B = pk2(E::get(rb[e / VEC], e % VEC), E::get(rb[e / VEC], e % VEC + 1));
+            up2(fma2(fma2(fma2(B, NEG1, A), SC, NZ), ONE, B), v[e], v[e + 1]);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = E::get(ra[e / VEC], e % VEC);
         }
-      } else {
+        if (a.timeshift_bias != 0.0f) {
+          const uint32_t bb = range_bits(a.ts_start - id0, a.ts_end - id0);
+          if (bb) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = E::get(ra[e / VEC], e % VEC);
-      }
-      if (a.timeshift_bias != 0.0f) {
-        const uint32_t bb = range_bits(a.ts_start - id0, a.ts_end - id0);
-        if (bb) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            if ((bb >> e) & 1u) v[e] = __fadd_rn(v[e], a.timeshift_bias);
-        }
-      }
-      if (!dv.pen_on) temp_chunk(a, dv, v, id0, t_row, y_row);
-      if (masks) {
-        uint32_t keep = range_bits(0, V - id0) & ~range_bits(a.ts_start - id0, mono_hi - id0);
-        if (gon) {
-          if (gbits) {
-            keep &= __ldg(gbits + (id0 >> 5)) >> (id0 & 31);
-          } else {
-            uint32_t g = 0;
-            const uint32_t ncls = (uint32_t)a.grammar_n_classes;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if (id0 + e < V) {
-                const uint32_t cl = __ldg(a.grammar_class_of + id0 + e);
-                g |= (cl < ncls ? (allow >> cl) & 1u : 0u) << e;
-              }
-            }
-            keep &= g;
+            for (int e = 0; e < 8; ++e)
+              if ((bb >> e) & 1u) v[e] = __fadd_rn(v[e], a.timeshift_bias);
           }
         }
+        if (!dv.pen_on) temp_chunk(a, dv, v, id0, t_row, y_row);
+        if (masks) {
+          const uint32_t keep = (uint32_t)((s < 8 ? km[0] : km[1]) >> (8 * (s & 7)));
 #pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = ((keep >> e) & 1u) ? v[e] : NEG;
+          for (int e = 0; e < 8; ++e) v[e] = ((keep >> e) & 1u) ? v[e] : NEG;
+        }
+        *(float4*)lo_of(c) = make_float4(v[0], v[1], v[2], v[3]);
+        *(float4*)hi_of(c) = make_float4(v[4], v[5], v[6], v[7]);
       }
-      *(float4*)lo_of(c) = make_float4(v[0], v[1], v[2], v[3]);
-      *(float4*)hi_of(c) = make_float4(v[4], v[5], v[6], v[7]);
     }
 
     // ---------------------------------------------------------- penalties: one lane per distinct history id
     if (dv.pen_on) {
       __syncwarp();
       const float rp = a.repetition_penalty, fp = a.frequency_penalty, pp = a.presence_penalty;
-      auto apply = [&](int32_t t) {
-        const uint32_t sh = 16u * (uint32_t)(t & 1);
-        const uint32_t old = atomicOr(cnt + (t >> 1), 0x8000u << sh);
-        if ((old >> sh) & 0x8000u) return;  // another lane owns this id
-        const float c = (float)((old >> sh) & 0x7fffu);
-        float* p = xat(t);
-        float x = *p;
-        if (rp != 1.0f) x = x < 0.0f ? __fmul_rn(x, rp) : __fdiv_rn(x, rp);
+      // repetition (x < 0 ? x * rp : x / rp), then frequency and presence; with
+      // rp = 1, fp = 0 or pp = 0 the step is the identity, so no step is skipped
+      auto pen_slow = [&](float x, float c) -> float {
+        if (rp != 1.0f) x = x < 0.0f ? __fmul_rn(x, rp) : (dv.rep_rcp != 0.0f ? div_by(x, rp, dv.rep_rcp) : div_rare(x, rp));
         if (fp != 0.0f) x = __fsub_rn(x, __fmul_rn(fp, c));
         if (pp != 0.0f) x = __fsub_rn(x, pp);
-        *p = x;
+        return x;
       };
+      auto pen = [&](int32_t t, uint32_t count) {
+        float* p = xat(t);
+        *p = pen_slow(*p, (float)count);
+      };
+      if (!long_hist) {
+        // the lane that counted an id first applies it, with the final count;
+        // per half of the window: loads first, then the arithmetic, then the stores
+        const float y = dv.rep_rcp;
 #pragma unroll
-      for (int k = 0; k < WHIST; ++k) {
-        const int pos = ah.hbase + lane + 32 * k;
-        const int32_t t = ah.hid[k];
-        if (pos >= a.penalty_start && pos < L && t >= 0 && t < V) apply(t);
-      }
-      for (int pos = a.penalty_start + lane; pos < ah.hbase; pos += 32) {  // long histories only
-        const int64_t t = load_id(a, row, pos);
-        if (t >= 0 && t < V) apply((int32_t)t);
+        for (int h0 = 0; h0 < WHIST; h0 += WHIST / 2) {
+          float xv[WHIST / 2];
+          uint32_t cw[WHIST / 2];
+#pragma unroll
+          for (int k = 0; k < WHIST / 2; ++k) {
+            const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
+            xv[k] = *xat(t);
+            cw[k] = cnt[t >> 1];
+          }
+          bool rare = false;
+#pragma unroll
+          for (int k = 0; k < WHIST / 2; ++k) {
+            const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
+            const float c = (float)((cw[k] >> (16 * (t & 1))) & 0xffffu);
+            const float x = xv[k];
+            const float ax = fabsf(x);
+            // x / rp by Markstein for normal-range positive x; other operands go out of line
+            const float q0 = __fmul_rn(x, y);
+            const float q = __fmaf_rn(__fmaf_rn(-q0, rp, x), y, q0);
+            rare |= ((own >> (h0 + k)) & 1u) && !(x < 0.0f) && !(y != 0.0f && ax >= 0x1p-60f && ax < 0x1p60f);
+            float r = x < 0.0f ? __fmul_rn(x, rp) : q;
+            r = __fsub_rn(r, __fmul_rn(fp, c));
+            xv[k] = __fsub_rn(r, pp);
+          }
+          if (__any_sync(FULL, rare)) {
+#pragma unroll
+            for (int k = 0; k < WHIST / 2; ++k) {
+              const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
+              xv[k] = pen_slow(*xat(t), (float)((cnt[t >> 1] >> (16 * (t & 1))) & 0xffffu));
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < WHIST / 2; ++k)
+            if ((own >> (h0 + k)) & 1u) *xat(ht[h0 + k]) = xv[k];
+        }
+      } else {
+        // long histories: owners are claimed through bit 15 of the counts (ids read again)
+        auto claim = [&](int32_t t) {
+          const uint32_t sh = 16u * (uint32_t)(t & 1);
+          const uint32_t old = atomicOr(cnt + (t >> 1), 0x8000u << sh);
+          if (!((old >> sh) & 0x8000u)) pen(t, (old >> sh) & 0x7fffu);
+        };
+#pragma unroll 1
+        for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
+          const int64_t t = load_id(a, row, pos);
+          if (t >= 0 && t < V) claim((int32_t)t);
+        }
       }
       __syncwarp();
       if (pen_temp) {
@@ -2295,6 +2479,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
     u64 qkept = 0;
     int32_t token = -1;
     int n = -1;  // survivors listed in lx / lid (-1: no list)
+    bool small = false;  // lx / lid hold the candidates (<= 64), not yet cut to the top k
 
     if (sel == MTR_SELECT_ARGMAX && !all_masked) {
       // lowest id of the maximum (of the first NaN when there is one)
@@ -2318,6 +2503,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       bool topk_done = false;
       if (!force_radix) {
         // bound: the chunk maxima in bins <= btau number >= k, so >= k scores lie within chi of the max
+#pragma unroll 1
         for (int i = lane * 4; i < WNB; i += 128) *(uint4*)(hc + i) = make_uint4(0u, 0u, 0u, 0u);
         __syncwarp();
 #pragma unroll
@@ -2364,7 +2550,11 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
             total += (int)__shfl_sync(FULL, incl, 31);
           }
           __syncwarp();
-          if (total <= WCAP) {
+          if (total <= 64) {
+            n = total;
+            small = true;
+            topk_done = true;
+          } else if (total <= WCAP) {
             n = total;
             // exact k-th value: fine histogram over the list, then the crossing bin
             const float s2 = (float)WNB / chi;
@@ -2373,13 +2563,16 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
               z = fminf(z, (float)(WNB - 1));
               return __float2int_rz(z);
             };
+#pragma unroll 1
             for (int i = lane * 4; i < WNB; i += 128) *(uint4*)(hc + i) = make_uint4(0u, 0u, 0u, 0u);
             __syncwarp();
+#pragma unroll 1
             for (int j = lane; j < n; j += 32) atomicAdd(hc + fbin(lx[j]), 1u);
             __syncwarp();
             u64 above2, w2;
             const int b2 = max(warp_crossing(hc, (u64)(k - 1), lane, above2, w2), 0);  // n >= k
             int m = 0;
+#pragma unroll 1
             for (int j0 = 0; j0 < n; j0 += 32) {
               const int j = j0 + lane;
               const bool in = j < n && fbin(lx[j]) == b2;
@@ -2392,9 +2585,11 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
             float my_tk = NEG;
             bool found = false;
             if (m <= WMINI) {
+#pragma unroll 1
               for (int j = lane; j < m; j += 32) {
                 const float xi = mx[j];
                 uint32_t gt = 0, ge = 0;
+#pragma unroll 1
                 for (int jj = 0; jj < m; ++jj) {
                   gt += mx[jj] > xi;
                   ge += mx[jj] >= xi;
@@ -2405,9 +2600,11 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
                 }
               }
             } else {
+#pragma unroll 1
               for (int j = lane; j < n; j += 32) {
                 const float xi = lx[j];
                 uint32_t gt = 0, ge = 0;
+#pragma unroll 1
                 for (int jj = 0; jj < n; ++jj) {
                   gt += lx[jj] > xi;
                   ge += lx[jj] >= xi;
@@ -2451,6 +2648,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       if (!topk_done) {
         // exact k-th over the whole row: count, then radix select over X
         uint32_t nf = 0;
+#pragma unroll 1
         for (int c = lane; c < nch; c += 32) {
           const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
           nf += finite_val(f0.x) + finite_val(f0.y) + finite_val(f0.z) + finite_val(f0.w) + finite_val(f1.x) +
@@ -2464,8 +2662,10 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           u64 above = 0, wlast = 0;
 #pragma unroll 1
           for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll 1
             for (int i = lane * 4; i < WNB; i += 128) *(uint4*)(hc + i) = make_uint4(0u, 0u, 0u, 0u);
             __syncwarp();
+#pragma unroll 1
             for (int id = lane; id < V; id += 32) {
               const float x = *xat(id);
               if (finite_val(x)) {
@@ -2486,6 +2686,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           if (nge <= (u64)WCAP && !force_radix) {
             // list the survivors in id order
             int base = 0;
+#pragma unroll 1
             for (int id0 = 0; id0 < V; id0 += 32) {
               const int id = id0 + lane;
               float x = NEG;
@@ -2505,19 +2706,88 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         }
       }
     }
-    if (!need_x_late && n >= 0) issue_next();  // X is no longer read by this row
+    if (!need_x_late && n >= 0) {  // X is no longer read by this row
+      issue_next();
+      if (nrow < a.num_rows) load_ahead(a, dv, nrow, lane, L, ah);
+    }
 
     // ---------------------------------------------------------- top-p and the draw
-    if (need_mass && n >= 0) {
+    if (small) {
+      // at most 64 candidates: one bitonic sort in canonical order (score desc,
+      // id asc) gives the k-th score, the top-p cut is a prefix scan, and a
+      // second sort of the kept entries by id gives the draw
+      const uint32_t k = (uint32_t)a.top_k;
+      const int j0 = 2 * lane, j1 = j0 + 1;
+      u64 a0 = j0 < n ? (((u64)fkey(lx[j0]) << 32) | (u64)(~(uint32_t)lid[j0])) : 0ull;
+      u64 a1 = j1 < n ? (((u64)fkey(lx[j1]) << 32) | (u64)(~(uint32_t)lid[j1])) : 0ull;
+      sort64_desc(a0, a1, lane);
+      const int p = (int)k - 1;
+      const u64 v0 = __shfl_sync(FULL, a0, p >> 1), v1 = __shfl_sync(FULL, a1, p >> 1);
+      const uint32_t tkey = (uint32_t)(((p & 1) ? v1 : v0) >> 32);
+      tk = key2f(tkey);
+      const bool s0 = a0 != 0ull && (uint32_t)(a0 >> 32) >= tkey, s1 = a1 != 0ull && (uint32_t)(a1 >> 32) >= tkey;
+      uint32_t q0 = 0, q1 = 0;
+      if (need_mass) {
+        expfx2(__fsub_rn(key2f((uint32_t)(a0 >> 32)), gmax), __fsub_rn(key2f((uint32_t)(a1 >> 32)), gmax), q0, q1);
+        q0 = s0 ? q0 : 0u;
+        q1 = s1 ? q1 : 0u;
+        const u64 lsum = (u64)q0 + q1;
+        const u64 incl = warp_incl_scan_u64(lsum, lane);
+        qkept = __shfl_sync(FULL, incl, 31);
+        int pcut = 64;
+        if (dv.topp_on) {
+          const double P = __dmul_rn((double)a.top_p, (double)qkept);
+          const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+          const u64 ab0 = incl - lsum, ab1 = ab0 + q0;
+          int my = -1;
+          u64 myq = 0;
+          if (q0 != 0u && ab0 <= plim && ab0 + q0 > plim) {
+            my = j0;
+            myq = ab0 + q0;
+          } else if (q1 != 0u && ab1 <= plim && ab1 + q1 > plim) {
+            my = j1;
+            myq = ab1 + q1;
+          }
+          const unsigned bal = __ballot_sync(FULL, my >= 0);
+          const int src = max(__ffs(bal) - 1, 0);
+          pcut = max(__shfl_sync(FULL, my, src), 0);
+          qkept = __shfl_sync(FULL, myq, src);
+          const int pn = min(pcut + 1, 63);
+          const u64 c0 = __shfl_sync(FULL, a0, pcut >> 1), c1 = __shfl_sync(FULL, a1, pcut >> 1);
+          const u64 n0 = __shfl_sync(FULL, a0, pn >> 1), n1 = __shfl_sync(FULL, a1, pn >> 1);
+          const u64 ck = (pcut & 1) ? c1 : c0, nk = (pn & 1) ? n1 : n0;
+          cut_x = key2f((uint32_t)(ck >> 32));
+          cut_id = (int32_t)(~(uint32_t)ck);
+          topp_cut = true;
+          if (pcut + 1 < 64 && nk != 0ull && (uint32_t)(nk >> 32) == (uint32_t)(ck >> 32)) status |= MTR_ROW_TIE_AT_CUT;
+        }
+        if (sel == MTR_SELECT_SAMPLE) {
+          const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
+          u64 b0 = (q0 != 0u && j0 <= pcut) ? (((u64)(uint32_t)a0 << 32) | q0) : 0ull;
+          u64 b1 = (q1 != 0u && j1 <= pcut) ? (((u64)(uint32_t)a1 << 32) | q1) : 0ull;
+          sort64_desc(b0, b1, lane);
+          const uint32_t w0 = (uint32_t)b0, w1 = (uint32_t)b1;
+          const u64 s2 = (u64)w0 + w1;
+          const u64 c = warp_incl_scan_u64(s2, lane) - s2;
+          int32_t my_tok = NO_ID;
+          if (w0 != 0u && c <= R && R < c + w0) my_tok = (int32_t)(~(uint32_t)(b0 >> 32));
+          else if (w1 != 0u && c + w0 <= R && R < c + w0 + w1) my_tok = (int32_t)(~(uint32_t)(b1 >> 32));
+          token = __reduce_min_sync(FULL, my_tok);
+        }
+      }
+    } else     if (need_mass && n >= 0) {
       // on the survivor list
+#pragma unroll 1
       for (int j = lane; j < n; j += 32) lq[j] = expfx(__fsub_rn(lx[j], gmax));
       __syncwarp();
       u64 tot = 0;
+#pragma unroll 1
       for (int j = lane; j < n; j += 32) tot += lq[j];
       tot = warp_sum_u64(tot);
       qkept = tot;
       // distance bins of the survivors (monotone in x): s3 spreads [0, d_max] over the bins
       float dmax = 0.0f;
+#pragma unroll 1
       for (int j = lane; j < n; j += 32) dmax = fmaxf(dmax, __fsub_rn(gmax, lx[j]));
       dmax = __uint_as_float(__reduce_max_sync(FULL, __float_as_uint(dmax)));  // non-negative: bits order as floats
       const float s3 = dmax > 0.0f ? (float)(WNB - 1) / dmax : 0.0f;
@@ -2529,8 +2799,10 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       if (dv.topp_on) {
         const double P = __dmul_rn((double)a.top_p, (double)tot);
         const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+#pragma unroll 1
         for (int i = lane * 2; i < WNB; i += 64) *(ulonglong2*)(hist + i) = make_ulonglong2(0ull, 0ull);
         __syncwarp();
+#pragma unroll 1
         for (int j = lane; j < n; j += 32)
           if (lq[j]) atomicAdd(hist + dbin3(lx[j]), (u64)lq[j]);
         __syncwarp();
@@ -2538,6 +2810,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         const int b3 = max(warp_crossing(hist, plim, lane, above3, w3), 0);  // plim < total
         // canonical order (score desc, id asc) inside the crossing bin
         int m = 0;
+#pragma unroll 1
         for (int j0 = 0; j0 < n; j0 += 32) {
           const int j = j0 + lane;
           const bool in = j < n && lq[j] != 0u && dbin3(lx[j]) == b3;
@@ -2556,10 +2829,12 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         u64 my_q = 0;
         bool found = false;
         if (m <= WMINI) {
+#pragma unroll 1
           for (int j = lane; j < m; j += 32) {
             const float xj = mx[j];
             const int32_t ij = mi[j];
             u64 am = above3;
+#pragma unroll 1
             for (int jj = 0; jj < m; ++jj)
               if (canon_before(mx[jj], mi[jj], xj, ij)) am += mq[jj];
             if (am <= plim && am + mq[j] > plim) {
@@ -2570,11 +2845,13 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
             }
           }
         } else {
+#pragma unroll 1
           for (int j = lane; j < n; j += 32) {
             const float xj = lx[j];
             const int32_t ij = lid[j];
             if (!lq[j]) continue;
             u64 am = 0;
+#pragma unroll 1
             for (int jj = 0; jj < n; ++jj)
               if (canon_before(lx[jj], lid[jj], xj, ij)) am += lq[jj];
             if (am <= plim && am + lq[j] > plim) {
@@ -2592,6 +2869,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         qkept = __shfl_sync(FULL, my_q, src);
         topp_cut = true;
         bool tie = false;
+#pragma unroll 1
         for (int j = lane; j < n; j += 32) tie |= lx[j] == cut_x && lid[j] > cut_id;
         if (__any_sync(FULL, tie)) status |= MTR_ROW_TIE_AT_CUT;
         __syncwarp();
@@ -2601,17 +2879,20 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
         int ish = 0;
         while ((VP >> ish) > WNB) ++ish;
+#pragma unroll 1
         for (int i = lane * 2; i < WNB; i += 64) *(ulonglong2*)(hist + i) = make_ulonglong2(0ull, 0ull);
         __syncwarp();
         auto kept = [&](int j) -> bool {
           return lq[j] != 0u && (!topp_cut || lx[j] > cut_x || (lx[j] == cut_x && lid[j] <= cut_id));
         };
+#pragma unroll 1
         for (int j = lane; j < n; j += 32)
           if (kept(j)) atomicAdd(hist + (lid[j] >> ish), (u64)lq[j]);
         __syncwarp();
         u64 above4, w4;
         const int b4 = max(warp_crossing(hist, R, lane, above4, w4), 0);  // R < qkept
         int m = 0;
+#pragma unroll 1
         for (int j0 = 0; j0 < n; j0 += 32) {
           const int j = j0 + lane;
           const bool in = j < n && kept(j) && (lid[j] >> ish) == b4;
@@ -2626,18 +2907,22 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         __syncwarp();
         int32_t my_tok = NO_ID;
         if (m <= WMINI) {
+#pragma unroll 1
           for (int j = lane; j < m; j += 32) {
             const int32_t ij = mi[j];
             u64 cm2 = above4;
+#pragma unroll 1
             for (int jj = 0; jj < m; ++jj)
               if (mi[jj] <= ij) cm2 += mq[jj];
             if (cm2 > R && cm2 - mq[j] <= R) my_tok = ij;
           }
         } else {
+#pragma unroll 1
           for (int j = lane; j < n; j += 32) {
             if (!kept(j)) continue;
             const int32_t ij = lid[j];
             u64 cm2 = 0;
+#pragma unroll 1
             for (int jj = 0; jj < n; ++jj)
               if (kept(jj) && lid[jj] <= ij) cm2 += lq[jj];
             if (cm2 > R && cm2 - lq[j] <= R) my_tok = ij;
@@ -2649,6 +2934,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       // dense path over the whole row (no usable survivor list)
       status |= MTR_ROW_SLOW_PATH;
       u64 tot = 0;
+#pragma unroll 1
       for (int id = lane; id < V; id += 32) {
         const float x = *xat(id);
         if (finite_val(x) && x >= tk) tot += expfx(__fsub_rn(x, gmax));
@@ -2662,8 +2948,10 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         u64 above = 0, lastw = 0;
 #pragma unroll 1
         for (int shift = 24; shift >= 0; shift -= 8) {
+#pragma unroll 1
           for (int i = lane * 2; i < WNB; i += 64) *(ulonglong2*)(hist + i) = make_ulonglong2(0ull, 0ull);
           __syncwarp();
+#pragma unroll 1
           for (int id = lane; id < V; id += 32) {
             const float x = *xat(id);
             if (finite_val(x) && x >= tk) {
@@ -2685,6 +2973,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         const float vstar = key2f(prefix);
         // the tie group at vstar shares one q
         uint32_t cnt_v = 0;
+#pragma unroll 1
         for (int id = lane; id < V; id += 32) cnt_v += (*xat(id) == vstar);
         const uint32_t lastc = max(__reduce_add_sync(FULL, cnt_v), 1u);
         const u64 qv = max(lastw / (u64)lastc, 1ull);
@@ -2696,6 +2985,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           // the nkeep-th smallest id of the tie group
           int32_t lo_id = -1;
           uint32_t seen = 0;
+#pragma unroll 1
           for (int id0 = 0; id0 < V && seen < nkeep; id0 += 32) {
             const int id = id0 + lane;
             const bool hit = id < V && *xat(id) == vstar;
@@ -2703,6 +2993,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
             const uint32_t cb = __popc(bm);
             if (seen + cb >= nkeep) {
               unsigned mm = bm;
+#pragma unroll 1
               for (uint32_t r = 1; r < nkeep - seen; ++r) mm &= mm - 1;
               lo_id = id0 + __ffs(mm) - 1;
             }
@@ -2718,6 +3009,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
         u64 run = 0;
         int32_t tok = -1;
+#pragma unroll 1
         for (int id0 = 0; id0 < V && tok < 0; id0 += 32) {
           const int id = id0 + lane;
           u64 q = 0;
@@ -2744,6 +3036,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       if (want_lp && clean) {
         if (!need_mass || sel == MTR_SELECT_ARGMAX) {
           u64 s = 0;
+#pragma unroll 1
           for (int id = lane; id < V; id += 32) {
             const float x = *xat(id);
             s += finite_val(x) ? expfx(__fsub_rn(x, gmax)) : 0u;
@@ -2754,6 +3047,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       }
       float* srow = a.out_scores ? a.out_scores + row * a.out_scores_row_stride : nullptr;
       float* lrow = want_lp ? a.out_logprobs + row * a.out_logprobs_row_stride : nullptr;
+#pragma unroll 1
       for (int i = lane * 4; i < V; i += 128) {
         const float4 f = *(const float4*)xat(i);
         const float v[4] = {f.x, f.y, f.z, f.w};
@@ -2786,7 +3080,10 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         }
       }
     }
-    issue_next();
+    if (!issued) {
+      issue_next();
+      if (nrow < a.num_rows) load_ahead(a, dv, nrow, lane, L, ah);
+    }
     if (lane == 0) {
       int32_t mm = mono;
       if (sel != MTR_SELECT_NONE) {
@@ -2803,7 +3100,6 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       if (a.mono_mode != MTR_MONO_OFF && a.mono_state) a.mono_state[row] = mm;
       if (a.out_status) a.out_status[row] = status;
     }
-    if (nrow < a.num_rows) load_ahead(a, dv, nrow, lane, L, ah);
     __syncwarp();  // this row's readers of the shared regions are done
   }
 }
@@ -2977,6 +3273,7 @@ static Derived derive(const MtrSamplerArgs& a) {
   while (((a.vocab - 1) >> d.id_shift) >= NB) ++d.id_shift;
   d.gwords = (a.vocab + 31) / 32;
   d.temp_rcp = 1.0f / a.temperature;
+  d.rep_rcp = (a.repetition_penalty >= 0x1p-30f && a.repetition_penalty <= 0x1p30f) ? 1.0f / a.repetition_penalty : 0.0f;
   d.neg_one = -1.0f;
   d.neg_zero = -0.0f;
   d.one = 1.0f;
