@@ -1966,12 +1966,21 @@ __device__ __forceinline__ int32_t narrow_raw(const MtrSamplerArgs& a, u64 raw) 
 __device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derived& dv, int64_t row, int lane, int L,
                                            WarpAhead& w) {
   w.hbase = L > WHIST * 32 ? L - WHIST * 32 : 0;
-  const bool need_hist = dv.pen_on || a.mono_mode == MTR_MONO_SCAN;
 #pragma unroll
-  for (int k = 0; k < WHIST; ++k) {
-    const int pos = w.hbase + lane + 32 * k;
-    w.hid[k] = RAW_NONE;
-    if (need_hist && pos < L) w.hid[k] = load_raw_id(a, row, pos);
+  for (int k = 0; k < WHIST; ++k) w.hid[k] = RAW_NONE;
+  if (dv.pen_on || a.mono_mode == MTR_MONO_SCAN) {
+    const int n = L - w.hbase - lane;  // this lane's positions: hbase + lane + 32 k < L
+    if (a.ids_dtype == MTR_IDS_I32) {
+      const uint32_t* p = (const uint32_t*)a.input_ids + row * a.ids_row_stride + w.hbase + lane;
+#pragma unroll
+      for (int k = 0; k < WHIST; ++k)
+        if (32 * k < n) w.hid[k] = (u64)__ldg(p + 32 * k);
+    } else {
+      const unsigned long long* p = (const unsigned long long*)a.input_ids + row * a.ids_row_stride + w.hbase + lane;
+#pragma unroll
+      for (int k = 0; k < WHIST; ++k)
+        if (32 * k < n) w.hid[k] = (u64)__ldg(p + 32 * k);
+    }
   }
   w.s0 = 0;
   w.s1 = 0;
@@ -2026,6 +2035,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
   float* mx = (float*)(lq + WCAP);
   int32_t* mi = (int32_t*)(mx + WMINI);
   uint32_t* mq = (uint32_t*)(mi + WMINI);
+  int32_t* ctr = (int32_t*)(mq + WMINI);  // list counter
   const int L = a.input_ids ? dv.ids_len : 0;
   const float NEG = neg_inf();
   const int sel = a.select_mode;
@@ -2228,31 +2238,64 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
     // keep bits of this lane's 16 chunks: slot s in bits 8s .. 8s+7 of km[s >> 3]
     u64 km[2] = {~0ull, ~0ull};
     if (masks) {
+      if (gon && gbits) {
+        // byte (lane & 3) of each slot's bitmap word, four slots per byte permute
+        const uint32_t b = (uint32_t)lane & 3u;
+        const uint32_t sel = b | ((b + 4u) << 4);
+        uint32_t w[4];
 #pragma unroll
-      for (int s = 0; s < NS; ++s) {
-        const int id0 = (s * 32 + lane) * 8;
-        uint32_t keep = 0;
-        if (id0 < V) {
-          keep = range_bits(0, V - id0) & ~range_bits(a.ts_start - id0, mono_hi - id0);
-          if (gon) {
-            if (gbits) {
-              keep &= gw[s] >> (id0 & 31);
-            } else {
-              uint32_t g = 0;
-              const uint32_t ncls = (uint32_t)a.grammar_n_classes;
+        for (int q = 0; q < 4; ++q)
+          w[q] = __byte_perm(__byte_perm(gw[4 * q], gw[4 * q + 1], sel), __byte_perm(gw[4 * q + 2], gw[4 * q + 3], sel),
+                             0x5410);
+        km[0] = (u64)w[0] | ((u64)w[1] << 32);
+        km[1] = (u64)w[2] | ((u64)w[3] << 32);
+      } else if (gon) {
+        const uint32_t ncls = (uint32_t)a.grammar_n_classes;
+#pragma unroll
+        for (int s = 0; s < NS; ++s) {
+          const int id0 = (s * 32 + lane) * 8;
+          uint32_t g = 0;
 #pragma unroll 1
-              for (int e = 0; e < 8; ++e) {
-                if (id0 + e < V) {
-                  const uint32_t cl = __ldg(a.grammar_class_of + id0 + e);
-                  g |= (cl < ncls ? (allow >> cl) & 1u : 0u) << e;
-                }
-              }
-              keep &= g;
+          for (int e = 0; e < 8; ++e) {
+            if (id0 + e < V) {
+              const uint32_t cl = __ldg(a.grammar_class_of + id0 + e);
+              g |= (cl < ncls ? (allow >> cl) & 1u : 0u) << e;
             }
           }
+          km[s >> 3] &= ~((u64)(~g & 0xffu) << (8 * (s & 7)));
         }
-        km[s >> 3] = (km[s >> 3] & ~(0xffull << (8 * (s & 7)))) | ((u64)(keep & 0xffu) << (8 * (s & 7)));
       }
+      // clear the bits of ids [lo, hi) in this lane's slots
+      auto clear_ids = [&](int lo, int hi) {
+        // whole chunks: slot s (ids 256 s + 8 lane ..) inside [lo, hi)
+        const int A = lo - 8 * lane, B = hi - 8 * lane - 8;
+        const int s_a = A <= 0 ? 0 : (A + 255) >> 8;
+        const int s_b = B < 0 ? -1 : min(B >> 8, NS - 1);
+        if (s_b >= s_a) {
+          const int b0 = 8 * s_a, b1 = 8 * (s_b + 1);  // bit range over the 128-bit mask
+          auto bits64 = [](int l, int h) -> u64 {
+            l = max(l, 0);
+            h = min(h, 64);
+            if (h <= l) return 0ull;
+            return (h >= 64 ? ~0ull : ((1ull << h) - 1ull)) & ~((1ull << l) - 1ull);
+          };
+          km[0] &= ~bits64(b0, b1);
+          km[1] &= ~bits64(b0 - 64, b1 - 64);
+        }
+        // partial chunks at either end belong to one lane each
+#pragma unroll
+        for (int end = 0; end < 2; ++end) {
+          const int x = end == 0 ? lo : hi - 1;
+          const int c = x >> 3;
+          if ((c & 31) == lane && (c >> 5) < NS) {
+            const int sl = c >> 5;
+            const uint32_t rb = range_bits(lo - 8 * c, hi - 8 * c);
+            km[sl >> 3] &= ~((u64)rb << (8 * (sl & 7)));
+          }
+        }
+      };
+      if (mono_hi > a.ts_start) clear_ids(a.ts_start, mono_hi);
+      if (V & 7) clear_ids(V, nch * 8);  // the ragged tail of the last chunk
     }
 
     // ---------------------------------------------------------- this row's logits
@@ -2502,41 +2545,61 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       const uint32_t k = (uint32_t)a.top_k;
       bool topk_done = false;
       if (!force_radix) {
-        // bound: the chunk maxima in bins <= btau number >= k, so >= k scores lie within chi of the max
-#pragma unroll 1
-        for (int i = lane * 4; i < WNB; i += 128) *(uint4*)(hc + i) = make_uint4(0u, 0u, 0u, 0u);
-        __syncwarp();
+        // bound: the chunk maxima in bins <= btau number >= k, so >= k scores lie
+        // within chi of the max.  btau by binary search over the 256 bins: each
+        // probe counts this lane's slots at or below it and sums over the warp.
+        uint32_t wbp[NS / 4];  // the slots' bins, four per word (255: empty slot)
 #pragma unroll
-        for (int s = 0; s < NS; ++s)
-          if (cm[s] > NEG) atomicAdd(hc + wbin(gmax, cm[s]), 1u);
-        __syncwarp();
-        u64 ab, wb;
-        const int btau = warp_crossing(hc, (u64)(k - 1), lane, ab, wb);
-        if (btau >= 0 && btau < WNB - 1) {  // the overflow bin bounds nothing
+        for (int q = 0; q < NS / 4; ++q) {
+          uint32_t w = 0;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const float x = cm[4 * q + r];
+            w |= (uint32_t)(x > NEG ? wbin(gmax, x) : WNB - 1) << (8 * r);
+          }
+          wbp[q] = w;
+        }
+        auto count_le = [&](int b) -> uint32_t {  // chunk maxima in bins <= b (b < 255)
+          uint32_t c = 0;
+#pragma unroll
+          for (int q = 0; q < NS / 4; ++q)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) c += ((wbp[q] >> (8 * r)) & 0xffu) <= (uint32_t)b;
+          return __reduce_add_sync(FULL, c);
+        };
+        int btau = WNB - 1;  // overflow: no bound
+        if (count_le(WNB - 2) >= k) {
+          int lo = 0, hi = WNB - 2;  // smallest b with count_le(b) >= k lies in [lo, hi]
+#pragma unroll 1
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (count_le(mid) >= k) hi = mid;
+            else lo = mid + 1;
+          }
+          btau = lo;
+        }
+        if (btau < WNB - 1) {  // the overflow bin bounds nothing
           const float chi = (float)(btau + 1) * (1.0f / WBIN_SCALE);
           uint32_t qual = 0;
 #pragma unroll
-          for (int s = 0; s < NS; ++s) qual |= (uint32_t)(cm[s] > NEG && wbin(gmax, cm[s]) <= btau) << s;
-          // each lane lists its qualifying chunks, one per round
-          int total = 0;
-          while (__any_sync(FULL, qual != 0u)) {
-            uint32_t cmask = 0;
-            float v[8];
-            int id0 = 0;
-            if (qual) {
-              const int s = __ffs(qual) - 1;
-              qual &= qual - 1u;
-              const int c = s * 32 + lane;
-              id0 = c * 8;
-              const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
-              v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
-              v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+          for (int q = 0; q < NS / 4; ++q)
 #pragma unroll
-              for (int e = 0; e < 8; ++e) cmask |= (uint32_t)(__fsub_rn(gmax, v[e]) < chi) << e;
-            }
-            const uint32_t cntl = __popc(cmask);
-            const uint32_t incl = warp_incl_scan_u32(cntl, lane);
-            int slot = total + (int)(incl - cntl);
+            for (int r = 0; r < 4; ++r) qual |= (uint32_t)(((wbp[q] >> (8 * r)) & 0xffu) <= (uint32_t)btau) << (4 * q + r);
+          // each lane lists the scores of its qualifying chunks within chi of the max
+          if (lane == 0) ctr[0] = 0;
+          __syncwarp();
+#pragma unroll 1
+          while (qual) {
+            const int s = __ffs(qual) - 1;
+            qual &= qual - 1u;
+            const int c = s * 32 + lane;
+            const int id0 = c * 8;
+            const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+            const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+            uint32_t cmask = 0;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) cmask |= (uint32_t)(__fsub_rn(gmax, v[e]) < chi) << e;
+            int slot = atomicAdd(ctr, __popc(cmask));
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               if ((cmask >> e) & 1u) {
@@ -2547,9 +2610,9 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
                 ++slot;
               }
             }
-            total += (int)__shfl_sync(FULL, incl, 31);
           }
           __syncwarp();
+          const int total = ctr[0];
           if (total <= 64) {
             n = total;
             small = true;
@@ -2762,17 +2825,25 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           if (pcut + 1 < 64 && nk != 0ull && (uint32_t)(nk >> 32) == (uint32_t)(ck >> 32)) status |= MTR_ROW_TIE_AT_CUT;
         }
         if (sel == MTR_SELECT_SAMPLE) {
+          // the smallest id whose id-ordered kept mass exceeds R, by binary search
+          // over ids (the kept mass only grows at kept ids)
           const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
-          u64 b0 = (q0 != 0u && j0 <= pcut) ? (((u64)(uint32_t)a0 << 32) | q0) : 0ull;
-          u64 b1 = (q1 != 0u && j1 <= pcut) ? (((u64)(uint32_t)a1 << 32) | q1) : 0ull;
-          sort64_desc(b0, b1, lane);
-          const uint32_t w0 = (uint32_t)b0, w1 = (uint32_t)b1;
-          const u64 s2 = (u64)w0 + w1;
-          const u64 c = warp_incl_scan_u64(s2, lane) - s2;
-          int32_t my_tok = NO_ID;
-          if (w0 != 0u && c <= R && R < c + w0) my_tok = (int32_t)(~(uint32_t)(b0 >> 32));
-          else if (w1 != 0u && c + w0 <= R && R < c + w0 + w1) my_tok = (int32_t)(~(uint32_t)(b1 >> 32));
-          token = __reduce_min_sync(FULL, my_tok);
+          const bool kp0 = q0 != 0u && j0 <= pcut, kp1 = q1 != 0u && j1 <= pcut;
+          const int i0 = (int)(~(uint32_t)a0), i1 = (int)(~(uint32_t)a1);
+          auto mass_le = [&](int m) -> u64 {  // kept mass of ids <= m (q < 2^31, <= 64 terms)
+            const uint32_t c0 = (kp0 && i0 <= m) ? q0 : 0u, c1 = (kp1 && i1 <= m) ? q1 : 0u;
+            const uint32_t lo16 = __reduce_add_sync(FULL, (c0 & 0xffffu) + (c1 & 0xffffu));
+            const uint32_t hi16 = __reduce_add_sync(FULL, (c0 >> 16) + (c1 >> 16));
+            return ((u64)hi16 << 16) + lo16;
+          };
+          int lo = 0, hi = V - 1;  // mass_le(V - 1) = qkept > R
+#pragma unroll 1
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (mass_le(mid) > R) hi = mid;
+            else lo = mid + 1;
+          }
+          token = lo;
         }
       }
     } else     if (need_mass && n >= 0) {
