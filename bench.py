@@ -269,6 +269,8 @@ def run_ours(args, dist: Dist):
                 step(i)
         torch.cuda.synchronize()
         return
+    info = sampler.launch_info(pool[0], history, upool[0])
+    kernel_name = "mtr::row_warp_kernel" if info.kernel == _native.KERNEL_ROW_WARP else "mtr::sampler_kernel"
     with ClockSampler(device.index) as clocks:
         ms, graph = time_graph(step, args.steps, stream, dist)
     ms = dist.max(ms)
@@ -317,7 +319,7 @@ def run_ours(args, dist: Dist):
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "fp32", "input_dtype": "bf16",
+            "vs_baseline": None, "dtype": "f32", "input_dtype": "bf16",
             "data": "synthetic: seeded N(0, 2^2) bf16 logits, uniform 512-id histories, random grammar table",
             "config": {"workload": WORKLOAD, "global_batch": PAIRS, "rows_per_gpu": 2 * pairs, "vocab": VOCAB,
                        "parallelism": f"row-sharded x{dist.world}, no collective",
@@ -325,7 +327,8 @@ def run_ours(args, dist: Dist):
                              f"> 3x L2)", "graph": f"{args.steps} launches captured in one CUDA graph"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": bytes_launch, "kernel": "mtr::sampler_kernel",
+                         "algorithmic_bytes_per_launch": bytes_launch, "kernel": kernel_name,
+                         "grid": info.grid, "threads": info.threads,
                          "avg_launch_us": per_launch_s * 1e6},
             "cpu_baseline": cpu,
             "e2e": {"value": PAIRS * e2e_steps / (e2e_ms / 1e3), "unit": "tokens/s",
@@ -439,7 +442,7 @@ def run_reference(args, dist: Dist):
               f"processors + softmax + multinomial), {args.steps} steps")
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "impl": "reference",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
             "data": "synthetic: seeded N(0, 2^2) bf16 logits, uniform 512-id histories",
             "config": {"workload": WORKLOAD, "global_batch": PAIRS, "sample_pairs_per_step": pairs},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},

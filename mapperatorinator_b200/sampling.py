@@ -286,6 +286,14 @@ class FusedSampler:
             a.uniforms = uniforms.data_ptr()
         return a
 
+    def launch_info(self, logits: torch.Tensor, input_ids: torch.Tensor | None = None,
+                    uniforms: torch.Tensor | None = None) -> N.MtrLaunchInfo:
+        """Kernel and geometry the next ``step`` with these tensors would launch
+        (``info.kernel``: 0 row-per-CTA, 1 row-per-warp)."""
+        if self._base.select_mode == N.SELECT_SAMPLE and uniforms is None:
+            uniforms = torch.zeros(self.num_rows, dtype=torch.float32, device=logits.device)
+        return N.query_args(self._args(logits, input_ids, uniforms))
+
     def step(self, logits: torch.Tensor, input_ids: torch.Tensor | None = None,
              uniforms: torch.Tensor | None = None, generator: torch.Generator | None = None) -> torch.Tensor:
         """Process one decoder step's logits ([B, V], or [2B, V] with CFG) and
