@@ -2035,7 +2035,6 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
   float* mx = (float*)(lq + WCAP);
   int32_t* mi = (int32_t*)(mx + WMINI);
   uint32_t* mq = (uint32_t*)(mi + WMINI);
-  int32_t* ctr = (int32_t*)(mq + WMINI);  // list counter
   const int L = a.input_ids ? dv.ids_len : 0;
   const float NEG = neg_inf();
   const int sel = a.select_mode;
@@ -2568,15 +2567,38 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           return __reduce_add_sync(FULL, c);
         };
         int btau = WNB - 1;  // overflow: no bound
-        if (count_le(WNB - 2) >= k) {
-          int lo = 0, hi = WNB - 2;  // smallest b with count_le(b) >= k lies in [lo, hi]
+        {
+          // the bound usually lies within 8 logits of the max: a 64-bin shared histogram
+          // of those bins (two per lane) and one scan find it
+          *(uint2*)(hc + 2 * lane) = make_uint2(0u, 0u);
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < NS / 4; ++q)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const uint32_t bq = (wbp[q] >> (8 * r)) & 0xffu;
+              if (bq < 64u) atomicAdd(hc + bq, 1u);
+            }
+          __syncwarp();
+          const uint2 hp = *(const uint2*)(hc + 2 * lane);
+          const uint32_t incl = warp_incl_scan_u32(hp.x + hp.y, lane);
+          const unsigned bal = __ballot_sync(FULL, incl >= k);
+          if (bal) {
+            const int l = __ffs(bal) - 1;  // first lane whose bins reach k
+            const uint32_t before = __shfl_sync(FULL, incl - hp.x - hp.y, l);
+            const uint32_t h0 = __shfl_sync(FULL, hp.x, l);
+            btau = 2 * l + (before + h0 >= k ? 0 : 1);
+          } else if (count_le(WNB - 2) >= k) {
+            int lo = 64, hi = WNB - 2;  // smallest b with count_le(b) >= k lies in [lo, hi]
 #pragma unroll 1
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (count_le(mid) >= k) hi = mid;
-            else lo = mid + 1;
+            while (lo < hi) {
+              const int mid = (lo + hi) >> 1;
+              if (count_le(mid) >= k) hi = mid;
+              else lo = mid + 1;
+            }
+            btau = lo;
           }
-          btau = lo;
+          __syncwarp();
         }
         if (btau < WNB - 1) {  // the overflow bin bounds nothing
           const float chi = (float)(btau + 1) * (1.0f / WBIN_SCALE);
@@ -2585,34 +2607,56 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           for (int q = 0; q < NS / 4; ++q)
 #pragma unroll
             for (int r = 0; r < 4; ++r) qual |= (uint32_t)(((wbp[q] >> (8 * r)) & 0xffu) <= (uint32_t)btau) << (4 * q + r);
-          // each lane lists the scores of its qualifying chunks within chi of the max
-          if (lane == 0) ctr[0] = 0;
-          __syncwarp();
+          // each lane lists the scores of its qualifying chunks within chi of the max:
+          // count (keeping each chunk's 8-bit hit mask), one warp scan for the offsets,
+          // then store at the final positions -- no shared counter, no overflow
+          int cl = 0;
+          u64 hm[2] = {0ull, 0ull};  // hit mask of slot s in byte s & 7 of hm[s >> 3]
+          {
+            uint32_t qq = qual;
 #pragma unroll 1
-          while (qual) {
-            const int s = __ffs(qual) - 1;
-            qual &= qual - 1u;
-            const int c = s * 32 + lane;
-            const int id0 = c * 8;
-            const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
-            const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
-            uint32_t cmask = 0;
+            while (qq) {
+              const int s = __ffs(qq) - 1;
+              qq &= qq - 1u;
+              const int c = s * 32 + lane;
+              const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+              const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+              uint32_t cmask = 0;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) cmask |= (uint32_t)(__fsub_rn(gmax, v[e]) < chi) << e;
-            int slot = atomicAdd(ctr, __popc(cmask));
+              for (int e = 0; e < 8; ++e) cmask |= (uint32_t)(__fsub_rn(gmax, v[e]) < chi) << e;
+              cl += __popc(cmask);
+              if (s < 8) hm[0] |= (u64)cmask << (8 * s);
+              else hm[1] |= (u64)cmask << (8 * (s - 8));
+            }
+          }
+          const uint32_t incl = warp_incl_scan_u32((uint32_t)cl, lane);
+          const int total = (int)__shfl_sync(FULL, incl, 31);
+          if (total <= WCAP) {
+            // small lists go straight to the sort's arrays
+            float* dx = total <= 64 ? mx : lx;
+            int32_t* di = total <= 64 ? mi : lid;
+            int pos = (int)incl - cl;
+            uint32_t qq = qual;
+#pragma unroll 1
+            while (qq) {
+              const int s = __ffs(qq) - 1;
+              qq &= qq - 1u;
+              const uint32_t cmask = (uint32_t)((s < 8 ? hm[0] : hm[1]) >> (8 * (s & 7))) & 0xffu;
+              if (cmask == 0u) continue;
+              const int c = s * 32 + lane;
+              const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+              const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              if ((cmask >> e) & 1u) {
-                if (slot < WCAP) {
-                  lx[slot] = v[e];
-                  lid[slot] = id0 + e;
+              for (int e = 0; e < 8; ++e)
+                if ((cmask >> e) & 1u) {
+                  const int p = pos + __popc(cmask & ((1u << e) - 1u));
+                  dx[p] = v[e];
+                  di[p] = c * 8 + e;
                 }
-                ++slot;
-              }
+              pos += __popc(cmask);
             }
           }
           __syncwarp();
-          const int total = ctr[0];
           if (total <= 64) {
             n = total;
             small = true;
@@ -2781,8 +2825,8 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       // second sort of the kept entries by id gives the draw
       const uint32_t k = (uint32_t)a.top_k;
       const int j0 = 2 * lane, j1 = j0 + 1;
-      u64 a0 = j0 < n ? (((u64)fkey(lx[j0]) << 32) | (u64)(~(uint32_t)lid[j0])) : 0ull;
-      u64 a1 = j1 < n ? (((u64)fkey(lx[j1]) << 32) | (u64)(~(uint32_t)lid[j1])) : 0ull;
+      u64 a0 = j0 < n ? (((u64)fkey(mx[j0]) << 32) | (u64)(~(uint32_t)mi[j0])) : 0ull;
+      u64 a1 = j1 < n ? (((u64)fkey(mx[j1]) << 32) | (u64)(~(uint32_t)mi[j1])) : 0ull;
       sort64_desc(a0, a1, lane);
       const int p = (int)k - 1;
       const u64 v0 = __shfl_sync(FULL, a0, p >> 1), v1 = __shfl_sync(FULL, a1, p >> 1);
