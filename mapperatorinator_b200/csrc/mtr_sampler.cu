@@ -406,17 +406,19 @@ __device__ __forceinline__ void find_crossing(const W* w, u64 lim, Cross* out) {
       out->total = total;
     }
     __syncwarp();
-    if (excl <= lim && lim < incl) {
-      u64 c = excl;
-      for (int i = 0; i < PER; ++i) {
-        const u64 wi = (u64)w[lane * PER + i];
-        if (c + wi > lim) {
-          out->bin = lane * PER + i;
-          out->above = c;
-          out->w = wi;
-          break;
-        }
-        c += wi;
+    // the crossing lane's segment, resolved by the whole warp (PER <= 32 bins)
+    const unsigned bal = __ballot_sync(FULL, excl <= lim && lim < incl);
+    if (bal) {
+      const int src = __ffs(bal) - 1;
+      const u64 seg_excl = __shfl_sync(FULL, excl, src);
+      const u64 wi = lane < PER ? (u64)w[src * PER + lane] : 0ull;
+      const u64 in2 = warp_incl_scan_u64(wi, lane) + seg_excl;
+      const unsigned b2 = __ballot_sync(FULL, lane < PER && in2 > lim);
+      const int l2 = __ffs(b2) - 1;  // the first such bin exists: lim < the segment's end
+      if (lane == l2) {
+        out->bin = src * PER + lane;
+        out->above = in2 - wi;
+        out->w = wi;
       }
     }
   }
@@ -3226,11 +3228,11 @@ struct Geo {
   int threads, ept, cs;
 };
 
-// Few rows of a small vocabulary: split each row over a cluster pair so more
-// SMs work on the step (latency); otherwise one CTA (or cluster) per row.
+// Few rows of a small vocabulary: one 512-thread CTA per row (8 ids per thread,
+// the shortest per-row latency); otherwise one CTA (or cluster) per row.
 static Geo pick_geo(int V, int64_t B, int sms) {
   if (V <= 4096) {
-    if (B * 2 <= sms) return {256, 8, 2};
+    if (B * 2 <= sms) return {512, 8, 1};
     return {256, 16, 1};
   }
   if (V <= 8192) return {256, 16, 2};
@@ -3478,7 +3480,7 @@ static cudaError_t launch_warp(const MtrSamplerArgs& a, const Derived& d, cudaSt
 
 template <typename Tin>
 static cudaError_t launch_dtype(const MtrSamplerArgs& a, const Derived& d, const Geo& g, int dyn, cudaStream_t s) {
-  if (g.threads == 256 && g.ept == 8 && g.cs == 2) return launch_t<Tin, 256, 8, 2>(a, d, dyn, s);
+  if (g.threads == 512 && g.ept == 8 && g.cs == 1) return launch_t<Tin, 512, 8, 1>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 1) return launch_t<Tin, 256, 16, 1>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 2) return launch_t<Tin, 256, 16, 2>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 4) return launch_t<Tin, 256, 16, 4>(a, d, dyn, s);

@@ -130,10 +130,10 @@ def test_zero_rows_is_a_noop(lib):
     assert lib.mtr_sampler_launch(ctypes.byref(a), None) == N.OK
 
 
-@pytest.mark.parametrize("vocab,rows,cs", [(1, 10, 2), (4096, 10, 2), (4096, 1000, 1), (4097, 10, 2), (8192, 10, 2),
+@pytest.mark.parametrize("vocab,rows,cs", [(1, 10, 1), (4096, 10, 1), (4096, 1000, 1), (4097, 10, 2), (8192, 10, 2),
                                            (16384, 10, 4), (65536, 10, 8), (131072, 10, 8)])
 def test_query_geometry(lib, vocab, rows, cs):
-    # few rows of a small vocabulary are split over a cluster pair (latency)
+    # few rows of a small vocabulary get one 512-thread CTA each (latency)
     info = N.query(vocab, rows, True)
     assert info.cluster_size == cs
     assert info.threads * info.elems_per_thread * info.cluster_size >= vocab
