@@ -425,6 +425,48 @@ __device__ __forceinline__ void find_crossing(const W* w, u64 lim, Cross* out) {
   __syncthreads();
 }
 
+// The same for the top-p cut: warp 0 sums the bins, derives the limit from the
+// total (P = top_p * total; HF: ceil(P) - 1, sample_fn: floor(P)) and finds its
+// crossing in one pass; out->total holds the total, out->pad the mode used.
+template <int NBINS, typename W>
+__device__ __forceinline__ void find_topp_crossing(const W* w, float top_p, int top_p_mode, Cross* out, u64* plim_out) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (tid < 32) {
+    constexpr int PER = NBINS / 32;
+    u64 s = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) s += (u64)w[lane * PER + ((i + lane) & (PER - 1))];  // rotated: no bank conflicts
+    const u64 incl = warp_incl_scan_u64(s, lane);
+    const u64 excl = incl - s;
+    const u64 total = __shfl_sync(FULL, incl, 31);
+    const double P = __dmul_rn((double)top_p, (double)total);
+    const u64 lim = top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+    if (lane == 0) {
+      out->bin = -1;
+      out->above = total;
+      out->w = 0;
+      out->total = total;
+      *plim_out = lim;
+    }
+    __syncwarp();
+    const unsigned bal = __ballot_sync(FULL, excl <= lim && lim < incl);
+    if (bal) {
+      const int src = __ffs(bal) - 1;
+      const u64 seg_excl = __shfl_sync(FULL, excl, src);
+      const u64 wi = lane < PER ? (u64)w[src * PER + lane] : 0ull;
+      const u64 in2 = warp_incl_scan_u64(wi, lane) + seg_excl;
+      const unsigned b2 = __ballot_sync(FULL, lane < PER && in2 > lim);
+      const int l2 = __ffs(b2) - 1;
+      if (lane == l2) {
+        out->bin = src * PER + lane;
+        out->above = in2 - wi;
+        out->w = wi;
+      }
+    }
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // shared memory
 // ---------------------------------------------------------------------------
@@ -460,6 +502,7 @@ struct alignas(16) Shared {
   int32_t cut_id;
   u64 qtot;
   u64 qkept;
+  u64 plim;  // top-p limit published by find_topp_crossing
   Cross cr;
   StatX stat;
   u64 cta_mass;
@@ -1446,13 +1489,9 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
             if (q[k]) atomicAdd(&sm.hmass[dbin(gmax, x[k])], (u64)q[k]);
           Clu<CS>::sync();
           const u64* hm = merged_masses(NB);
-          // total first, then the crossing of plim
-          find_crossing<NB>(hm, ~0ull - 1ull, &sm.cr);
-          const u64 tot = sm.cr.total;
-          const double P = __dmul_rn((double)a.top_p, (double)tot);
-          const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
-          __syncthreads();
-          find_crossing<NB>(hm, plim, &sm.cr);
+          // total, the limit it implies, and the crossing of the limit, in one pass
+          find_topp_crossing<NB>(hm, a.top_p, a.top_p_mode, &sm.cr, &sm.plim);
+          const u64 plim = sm.plim;
           const int bstar = max(sm.cr.bin, 0);  // plim < total since top_p < 1
           const u64 w_above = sm.cr.above;
           const float lo = (float)bstar * (1.0f / BIN_SCALE), hi = (float)(bstar + 1) * (1.0f / BIN_SCALE);
@@ -1465,7 +1504,27 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
           collect<CS, EPT>(sm, mask, x, q, true, id_of, lane);
           const int n = merge_lists();
           if (n <= CAP && !force_radix) {
-            if (tid < n) {
+            if (n <= 32) {
+              // one warp: lane j holds candidate j and sums the mass canonically before it
+              if (warp == 0) {
+                const float xj = lane < n ? lx[lane] : 0.0f;
+                const int32_t ij = lane < n ? lid[lane] : NO_ID;
+                const uint32_t qj = lane < n ? lq[lane] : 0u;
+                u64 aj = w_above;
+#pragma unroll 4
+                for (int i = 0; i < n; ++i) {
+                  const float xi = __shfl_sync(FULL, xj, i);
+                  const int32_t ii = __shfl_sync(FULL, ij, i);
+                  const uint32_t qi = __shfl_sync(FULL, qj, i);
+                  aj += canon_before(xi, ii, xj, ij) ? (u64)qi : 0ull;
+                }
+                if (lane < n && aj <= plim && aj + qj > plim) {
+                  sm.cut_x = xj;
+                  sm.cut_id = ij;
+                  sm.qkept = aj + qj;
+                }
+              }
+            } else if (tid < n) {
               const float xi = lx[tid];
               const int32_t ii = lid[tid];
               const u64 qi = lq[tid];
