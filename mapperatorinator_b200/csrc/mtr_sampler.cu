@@ -428,14 +428,14 @@ __device__ __forceinline__ void find_crossing(const W* w, u64 lim, Cross* out) {
 // The same for the top-p cut: warp 0 sums the bins, derives the limit from the
 // total (P = top_p * total; HF: ceil(P) - 1, sample_fn: floor(P)) and finds its
 // crossing in one pass; out->total holds the total, out->pad the mode used.
-template <int NBINS, typename W>
-__device__ __forceinline__ void find_topp_crossing(const W* w, float top_p, int top_p_mode, Cross* out, u64* plim_out) {
+template <int NBINS, typename WF>
+__device__ __forceinline__ void find_topp_crossing(WF w, float top_p, int top_p_mode, Cross* out, u64* plim_out) {
   const int tid = threadIdx.x, lane = tid & 31;
   if (tid < 32) {
     constexpr int PER = NBINS / 32;
     u64 s = 0;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) s += (u64)w[lane * PER + ((i + lane) & (PER - 1))];  // rotated: no bank conflicts
+    for (int i = 0; i < PER; ++i) s += w(lane * PER + ((i + lane) & (PER - 1)));  // rotated: no bank conflicts
     const u64 incl = warp_incl_scan_u64(s, lane);
     const u64 excl = incl - s;
     const u64 total = __shfl_sync(FULL, incl, 31);
@@ -453,7 +453,7 @@ __device__ __forceinline__ void find_topp_crossing(const W* w, float top_p, int 
     if (bal) {
       const int src = __ffs(bal) - 1;
       const u64 seg_excl = __shfl_sync(FULL, excl, src);
-      const u64 wi = lane < PER ? (u64)w[src * PER + lane] : 0ull;
+      const u64 wi = lane < PER ? w(src * PER + lane) : 0ull;
       const u64 in2 = warp_incl_scan_u64(wi, lane) + seg_excl;
       const unsigned b2 = __ballot_sync(FULL, lane < PER && in2 > lim);
       const int l2 = __ffs(b2) - 1;
@@ -600,6 +600,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   static_assert(EPT <= 32, "per-thread element masks are 32 bits");
   static_assert(THREADS >= CAP, "one thread per list entry");
   static_assert(NCH <= 4, "per-chunk partials");
+  static_assert(TILE <= (1 << 14), "the split u32 mass histogram holds <= 2^14 elements per CTA");
 
   __shared__ Shared<CS> sm;
   extern __shared__ __align__(16) uint8_t dsm[];
@@ -1484,13 +1485,37 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
           zero_hmass();
           if (tid == 0) sm.nc = 0;
           __syncthreads();
+          // mass histogram as two u32 halves (low / high 16 bits of q): native
+          // 32-bit shared atomics, exact for a CTA's <= 2^14 elements
+          uint32_t* hlo = (uint32_t*)sm.hmass;
+          uint32_t* hhi = hlo + NB;
 #pragma unroll
-          for (int k = 0; k < EPT; ++k)
-            if (q[k]) atomicAdd(&sm.hmass[dbin(gmax, x[k])], (u64)q[k]);
+          for (int k = 0; k < EPT; ++k) {
+            if (q[k]) {
+              const int b = dbin(gmax, x[k]);
+              atomicAdd(hlo + b, q[k] & 0xffffu);
+              atomicAdd(hhi + b, q[k] >> 16);
+            }
+          }
           Clu<CS>::sync();
-          const u64* hm = merged_masses(NB);
           // total, the limit it implies, and the crossing of the limit, in one pass
-          find_topp_crossing<NB>(hm, a.top_p, a.top_p_mode, &sm.cr, &sm.plim);
+          if constexpr (CS == 1) {
+            find_topp_crossing<NB>([&](int i) -> u64 { return (u64)hlo[i] + ((u64)hhi[i] << 16); }, a.top_p,
+                                   a.top_p_mode, &sm.cr, &sm.plim);
+          } else {
+            for (int i = tid; i < NB; i += THREADS) {
+              u64 m = 0;
+#pragma unroll
+              for (int r = 0; r < CS; ++r) {
+                const uint32_t* rl = (const uint32_t*)Clu<CS>::at(sm.hmass, r);
+                m += (u64)rl[i] + ((u64)rl[NB + i] << 16);
+              }
+              sm.hmass_m[i] = m;
+            }
+            __syncthreads();
+            find_topp_crossing<NB>([&](int i) -> u64 { return sm.hmass_m[i]; }, a.top_p, a.top_p_mode, &sm.cr,
+                                   &sm.plim);
+          }
           const u64 plim = sm.plim;
           const int bstar = max(sm.cr.bin, 0);  // plim < total since top_p < 1
           const u64 w_above = sm.cr.above;
