@@ -186,6 +186,48 @@ __device__ __forceinline__ void div_by2(float& x0, float& x1, float t, float y) 
   x1 = ok1 ? q1 : (pass1 ? x1 : q1);
 }
 
+// maxima that return NaN when any input is NaN (three-input form: sm_100)
+__device__ __forceinline__ float fmax3n(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmax2n(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+__device__ __noinline__ void div_chunk_rare(float (&v)[8], float t, float y) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = div_by(v[e], t, y);
+}
+
+// x / t for a chunk (y = RN(1/t)): Markstein on pairs when every value that is
+// not -inf lies in [2^-60, 2^60) (-inf passes through), the IEEE divide per
+// element otherwise.
+__device__ __forceinline__ void div_chunk(float (&v)[8], float t, float y) {
+  float w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = v[e] == neg_inf() ? 1.0f : fabsf(v[e]);
+  const float amax = fmax3n(fmax3n(w[0], w[1], w[2]), fmax3n(w[3], w[4], w[5]), fmax2n(w[6], w[7]));
+  const float amin = fminf(fminf(fminf(w[0], w[1]), fminf(w[2], w[3])), fminf(fminf(w[4], w[5]), fminf(w[6], w[7])));
+  if (amax < 0x1p60f && amin >= 0x1p-60f) {
+    const u64 Y = pk2(y, y), NT = pk2(-t, -t);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const u64 Xv = pk2(v[e], v[e + 1]);
+      const u64 Q0 = mul2(Xv, Y);
+      float q0, q1;
+      up2(fma2(fma2(Q0, NT, Xv), Y, Q0), q0, q1);
+      v[e] = v[e] == neg_inf() ? v[e] : q0;
+      v[e + 1] = v[e + 1] == neg_inf() ? v[e + 1] : q1;
+    }
+  } else {
+    div_chunk_rare(v, t, y);
+  }
+}
+
 // order-preserving key of a non-NaN float (-0 and +0 share a key)
 __device__ __forceinline__ uint32_t fkey(float x) {
   uint32_t u = __float_as_uint(x);
@@ -207,18 +249,6 @@ __device__ __forceinline__ int dbin(float mx, float x) {
 }
 
 __device__ __forceinline__ bool finite_val(float x) { return fabsf(x) < pos_inf(); }
-
-// maxima that return NaN when any input is NaN (three-input form: sm_100)
-__device__ __forceinline__ float fmax3n(float a, float b, float c) {
-  float d;
-  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ float fmax2n(float a, float b) {
-  float d;
-  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
-  return d;
-}
 
 // Hint: pull [p, p + bytes) into L2 with one bulk prefetch (16-byte granules
 // fully inside the range; nothing is read into the SM).
@@ -532,6 +562,7 @@ struct alignas(16) Shared {
   int32_t nid[MINI];
   uint32_t nq[MINI];
   uint8_t ckeep[CAP];
+  uint32_t gword[512];  // this CTA's words of the previous token's grammar bitmap (tile / 32 <= 512)
 };
 
 // Host-derived constants of one launch.
@@ -651,16 +682,18 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     __syncthreads();
     mono = sm.red_i[0];
   }
-  // independent dependent-load chains on separate lanes of warp 0
-  if (warp == 0) {
-    if (lane == 0) {
+  // independent dependent-load chains, each on lane 0 of its own warp (lanes of one
+  // warp would run the divergent chains one after another): grammar on warp 0,
+  // monotonic state on warp 1, conditional temperature on warp 2, uniform on warp 3
+  if (lane == 0) {
+    if (warp == 1) {
       if (a.mono_mode == MTR_MONO_STATE) {
         mono = a.mono_state[row];
         if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) mono = mono_update(a, mono, load_id(a, row, L - 1));
       }
       sm.mono = mono;
       sm.mono_hi = mono >= 0 ? (int32_t)min((int64_t)a.ts_end, (int64_t)a.ts_start + mono) : -1;
-    } else if (lane == 1) {
+    } else if (warp == 0) {
       uint32_t status = 0, allow = 0xffffffffu;
       int gon = 0;
       const uint32_t* gbits = nullptr;
@@ -673,8 +706,8 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
           const uint32_t c = __ldg(a.grammar_class_of + prev);
           if (c < (uint32_t)a.grammar_n_classes) {
             gon = 1;
-            allow = __ldg(a.grammar_allow + c);
             if (a.grammar_vocab_bits) gbits = a.grammar_vocab_bits + (size_t)c * dv.gwords;
+            else allow = __ldg(a.grammar_allow + c);  // the class-byte path needs the allow row
           } else {
             status |= MTR_ROW_BAD_ID;
           }
@@ -684,7 +717,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       sm.grammar_on = gon;
       sm.gbits = gbits;
       sm.status_g = status;
-    } else if (lane == 2) {
+    } else if (warp == 2) {
       float t = a.temperature, y = dv.temp_rcp;
       if (a.temp_mode == MTR_TEMP_ROW_CONDITIONAL) {
         for (int c = 0; c < a.n_cond; ++c) {
@@ -700,7 +733,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       }
       sm.t_row = t;
       sm.t_rcp = y;
-    } else if (lane == 3) {
+    } else if (warp == 3) {
       float u = 0.0f;
       uint32_t status = 0;
       if (sel == MTR_SELECT_SAMPLE) {
@@ -715,7 +748,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       }
       sm.u = u;
       sm.status_u = status;
-    } else if (lane == 4) {
+    } else if (warp == 4) {
       sm.status = 0u;
       sm.n_uniq = 0;
       sm.nc = 0;
@@ -781,6 +814,16 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       x[k] = v;
     }
   }
+  if (warp == 0) {
+    // warp 0 stages this CTA's words of the grammar bitmap, so the masks below
+    // read shared memory instead of a fourth dependent global load
+    __syncwarp();
+    const uint32_t* gb = sm.gbits;
+    if (gb) {
+      const int w0 = base >> 5, nw = min(TILE >> 5, dv.gwords - w0);
+      for (int k = lane; k < nw; k += 32) sm.gword[k] = __ldg(gb + w0 + k);
+    }
+  }
   __syncthreads();  // prologue scalars visible
 
   // ------------------------------------------------------------ masks (per 8-id chunk)
@@ -801,7 +844,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         keep &= ~range_bits(ts0 - id0, mono_hi - id0);    // monotonic: [ts0, mono_hi) removed
         if (gon && id0 < V) {
           if (gbits) {
-            keep &= __ldg(gbits + (id0 >> 5)) >> (id0 & 31);  // id0 % VEC == 0: the chunk sits in one word
+            keep &= sm.gword[(id0 - base) >> 5] >> (id0 & 31);  // id0 % VEC == 0: the chunk sits in one word
           } else {
             uint32_t g = 0;
             if (dv.cls_vec) {
@@ -942,8 +985,17 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       }
       if (uniform_chunk) {
         if (t0 != 1.0f) {
+          if constexpr (VEC == 8) {
+            float v8[8];
 #pragma unroll
-          for (int e = 0; e < VEC; e += 2) div_by2(x[j * VEC + e], x[j * VEC + e + 1], t0, y0);
+            for (int e = 0; e < 8; ++e) v8[e] = x[j * VEC + e];
+            div_chunk(v8, t0, y0);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) x[j * VEC + e] = v8[e];
+          } else {
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) div_by2(x[j * VEC + e], x[j * VEC + e + 1], t0, y0);
+          }
         }
       } else {
 #pragma unroll
@@ -1930,36 +1982,6 @@ __device__ __forceinline__ int warp_crossing(const W* h, u64 lim, int lane, u64&
   return __shfl_sync(FULL, my_b, src);
 }
 
-__device__ __noinline__ void div_chunk_rare(float (&v)[8], float t, float y) {
-#pragma unroll
-  for (int e = 0; e < 8; ++e) v[e] = div_by(v[e], t, y);
-}
-
-// x / t for a chunk (y = RN(1/t)): Markstein on pairs when every value that is
-// not -inf lies in [2^-60, 2^60) (-inf passes through), the IEEE divide per
-// element otherwise.
-__device__ __forceinline__ void div_chunk(float (&v)[8], float t, float y) {
-  float w[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) w[e] = v[e] == neg_inf() ? 1.0f : fabsf(v[e]);
-  const float amax = fmax3n(fmax3n(w[0], w[1], w[2]), fmax3n(w[3], w[4], w[5]), fmax2n(w[6], w[7]));
-  const float amin = fminf(fminf(fminf(w[0], w[1]), fminf(w[2], w[3])), fminf(fminf(w[4], w[5]), fminf(w[6], w[7])));
-  if (amax < 0x1p60f && amin >= 0x1p-60f) {
-    const u64 Y = pk2(y, y), NT = pk2(-t, -t);
-#pragma unroll
-    for (int e = 0; e < 8; e += 2) {
-      const u64 Xv = pk2(v[e], v[e + 1]);
-      const u64 Q0 = mul2(Xv, Y);
-      float q0, q1;
-      up2(fma2(fma2(Q0, NT, Xv), Y, Q0), q0, q1);
-      v[e] = v[e] == neg_inf() ? v[e] : q0;
-      v[e + 1] = v[e + 1] == neg_inf() ? v[e + 1] : q1;
-    }
-  } else {
-    div_chunk_rare(v, t, y);
-  }
-}
-
 // a chunk that a column-range edge splits: element by element (out of line)
 __device__ __noinline__ void temp_chunk_split(const MtrSamplerArgs& a, const Derived& dv, float (&v)[8], int id0) {
   for (int e = 0; e < 8; ++e) {
@@ -2032,6 +2054,7 @@ struct WarpAhead {
   u64 s0;          // lane 0: mono_state; lane 1: previous token (raw)
   u64 s1;          // lane 0: last id (mono update); lane 3: uniform bits
   u64 cond[MTR_MAX_COND_TEMPS];  // lane 2: raw ids at L - cond_offset[c]
+  uint32_t cls;    // lane 1: grammar class of the previous token, looked up one row ahead
 };
 constexpr u64 RAW_NONE = 0x8000000000000000ull;  // an id that lies outside int32: never valid
 
@@ -2047,6 +2070,22 @@ __device__ __forceinline__ int64_t raw_id(const MtrSamplerArgs& a, u64 raw) {
 __device__ __forceinline__ int32_t narrow_raw(const MtrSamplerArgs& a, u64 raw) {
   const int64_t t = raw_id(a, raw);
   return (t >= INT32_MIN && t <= INT32_MAX) ? (int32_t)t : INT32_MIN;
+}
+
+// the previous token of the row ahead (lane 1; -1: none)
+__device__ __forceinline__ int64_t ahead_prev(const MtrSamplerArgs& a, const WarpAhead& w) {
+  if (w.s0 == RAW_NONE) return -1;
+  return (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) ? raw_id(a, w.s0) : (int64_t)(int32_t)(uint32_t)w.s0;
+}
+// second step of the row-ahead loads, issued once the first step has landed:
+// the class of the previous token (lane 1), so the row's prologue has no
+// dependent global load on the grammar path
+__device__ __forceinline__ void load_ahead_class(const MtrSamplerArgs& a, int lane, int V, WarpAhead& w) {
+  w.cls = 0xffffffffu;
+  if (lane == 1 && a.grammar_class_of) {
+    const int64_t prev = ahead_prev(a, w);
+    if (prev >= 0 && prev < V) w.cls = __ldg(a.grammar_class_of + prev);
+  }
 }
 
 __device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derived& dv, int64_t row, int lane, int L,
@@ -2148,7 +2187,10 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
   uint32_t parity = 0;
   if (bulk && lane == 0 && row < a.num_rows) issue_copy(row);
   WarpAhead ah;
-  if (row < a.num_rows) load_ahead(a, dv, row, lane, L, ah);
+  if (row < a.num_rows) {
+    load_ahead(a, dv, row, lane, L, ah);
+    load_ahead_class(a, lane, V, ah);
+  }
 
 #pragma unroll 1
   for (; row < a.num_rows; row += gridDim.x) {
@@ -2180,16 +2222,14 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         m0 = (int32_t)(uint32_t)ah.s0;
         if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) m0 = mono_update(a, m0, raw_id(a, ah.s1));
       } else if (lane == 1 && a.grammar_class_of) {
-        const int64_t prev = ah.s0 == RAW_NONE ? -1
-                             : ((a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) ? raw_id(a, ah.s0)
-                                                                          : (int64_t)(int32_t)(uint32_t)ah.s0);
+        const int64_t prev = ahead_prev(a, ah);
         if (prev >= V) st |= MTR_ROW_BAD_ID;
         if (prev >= 0 && prev < V) {
-          const uint32_t c = __ldg(a.grammar_class_of + prev);
+          const uint32_t c = ah.cls;
           if (c < (uint32_t)a.grammar_n_classes) {
             g = 1;
-            al = __ldg(a.grammar_allow + c);
             if (a.grammar_vocab_bits) gb = (u64)(a.grammar_vocab_bits + (size_t)c * dv.gwords);
+            else al = __ldg(a.grammar_allow + c);  // the class-byte path needs the allow row
           } else {
             st |= MTR_ROW_BAD_ID;
           }
@@ -3301,6 +3341,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       if (a.mono_mode != MTR_MONO_OFF && a.mono_state) a.mono_state[row] = mm;
       if (a.out_status) a.out_status[row] = status;
     }
+    if (nrow < a.num_rows) load_ahead_class(a, lane, V, ah);  // the row-ahead values have landed by now
     __syncwarp();  // this row's readers of the shared regions are done
   }
 }
