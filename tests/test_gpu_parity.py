@@ -304,3 +304,58 @@ def test_column_temperature_ranges_split_chunks(cuda_device):
                      select_mode=N.SELECT_SAMPLE, top_p=0.9, uniforms=rng.random(64, dtype=np.float32),
                      want_scores=True, want_logprobs=True)
     assert_parity(s, cuda_device)
+
+
+# ---------------------------------------------------------------- penalty paths of the row-per-warp kernel
+@pytest.mark.parametrize("ids_dtype", [np.int64, np.int32])
+def test_long_history_penalty_window(cuda_device, ids_dtype):
+    # histories longer than the 512 ids a warp keeps in registers, penalty windows
+    # that start inside the history, repeated ids, int32 and int64 ids
+    rng = np.random.default_rng(121)
+    rows, V = 320, 4096
+    x = W.bf16_bits(rng.normal(0, 2, size=(rows, V)).astype(np.float32))
+    for L, start in ((1500, 0), (1500, 700), (700, 650), (513, 0)):
+        ids = rng.integers(0, V, size=(rows, L)).astype(ids_dtype)
+        ids[:, -40:] = rng.integers(0, 64, size=(rows, 40))
+        s = W.StepInputs(logits=x, dtype="bf16", num_rows=rows, input_ids=ids, penalty_start=start,
+                         repetition_penalty=1.2, frequency_penalty=0.3, presence_penalty=0.05,
+                         select_mode=N.SELECT_SAMPLE, top_k=40, top_p=0.9,
+                         uniforms=rng.random(rows, dtype=np.float32), want_scores=True)
+        assert_parity(s, cuda_device)
+
+
+@pytest.mark.parametrize("rp", [1.2, 0.5, 2.0 ** 31, 2.0 ** -31])
+def test_penalty_rare_operands(cuda_device, rp):
+    # signed zeros and huge scores at penalised ids (the divide leaves the fast
+    # path) and repetition penalties on both sides of the fast divide's range
+    rng = np.random.default_rng(131)
+    rows, V = 320, 4096
+    xf = rng.normal(0, 2, size=(rows, V)).astype(np.float32)
+    ids = rng.integers(0, V, size=(rows, 256)).astype(np.int64)
+    r = np.arange(rows)[:, None]
+    xf[r, ids[:, :6]] = 0.0
+    xf[r, ids[:, 6:9]] = -0.0
+    xf[r, ids[:, 9:11]] = 3.0e30
+    s = W.StepInputs(logits=W.bf16_bits(xf), dtype="bf16", num_rows=rows, input_ids=ids, repetition_penalty=rp,
+                     frequency_penalty=0.1, presence_penalty=0.2, select_mode=N.SELECT_SAMPLE, top_k=50, top_p=0.95,
+                     uniforms=rng.random(rows, dtype=np.float32), want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+
+
+@pytest.mark.parametrize("temp", ["scalar", "conditional", "columns"])
+def test_penalties_then_temperature(cuda_device, temp):
+    # penalties come before temperature: a temperature pass follows the penalty update
+    rng = np.random.default_rng(141)
+    rows, V = 320, 4096
+    x = W.bf16_bits(rng.normal(0, 2, size=(2 * rows, V)).astype(np.float32))
+    ids = rng.integers(0, V, size=(rows, 300)).astype(np.int64)
+    kw = dict(temperature=0.7)
+    if temp == "conditional":
+        ids[: rows // 2, -1] = 5
+        kw = dict(temp_mode=N.TEMP_ROW_CONDITIONAL, temperature=1.0, cond=[(0.6, 1, G.bits_for([5, 6], V))])
+    elif temp == "columns":
+        kw = dict(temp_mode=N.TEMP_COLUMN_RANGES, temperature=1.0, col_ranges=[(0, 2003, 0.9), (2003, 3001, 1.7)])
+    s = W.StepInputs(logits=x, dtype="bf16", num_rows=rows, cfg_scale=1.5, input_ids=ids, repetition_penalty=1.1,
+                     frequency_penalty=0.2, presence_penalty=0.1, select_mode=N.SELECT_SAMPLE, top_k=50, top_p=0.95,
+                     uniforms=rng.random(rows, dtype=np.float32), want_scores=True, **kw)
+    assert_parity(s, cuda_device)
