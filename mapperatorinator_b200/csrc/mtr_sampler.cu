@@ -2051,18 +2051,19 @@ __device__ __forceinline__ void sort64_desc(u64& a0, u64& a1, int lane) {
 struct WarpAhead {
   u64 hid[WHIST];  // raw ids at positions hbase + lane + 32k (int32 ids zero-extended)
   int32_t hbase;
-  u64 s0;          // lane 0: mono_state; lane 1: previous token (raw)
-  u64 s1;          // lane 0: last id (mono update); lane 3: uniform bits
-  u64 cond[MTR_MAX_COND_TEMPS];  // lane 2: raw ids at L - cond_offset[c]
+  // per-row scalars, each loaded straight into its own register (a conversion
+  // right after the load would wait for it)
+  int32_t mono;    // lane 0: mono_state[row]
+  int32_t prev;    // lane 1: prev_token[row]
+  uint32_t ubits;  // lane 3: uniforms[row]
+  uint32_t last32; // lane 0 / 1: input_ids[row, L - 1] (int32 ids)
+  u64 last64;      // lane 0 / 1: input_ids[row, L - 1] (int64 ids)
+  uint32_t cond32[MTR_MAX_COND_TEMPS];  // lane 2: input_ids[row, L - cond_offset[c]] (int32 ids)
+  u64 cond64[MTR_MAX_COND_TEMPS];       // lane 2: the same (int64 ids)
   uint32_t cls;    // lane 1: grammar class of the previous token, looked up one row ahead
 };
 constexpr u64 RAW_NONE = 0x8000000000000000ull;  // an id that lies outside int32: never valid
 
-__device__ __forceinline__ u64 load_raw_id(const MtrSamplerArgs& a, int64_t row, int64_t pos) {
-  const int64_t off = row * a.ids_row_stride + pos;
-  if (a.ids_dtype == MTR_IDS_I32) return (u64)__ldg((const uint32_t*)a.input_ids + off);
-  return (u64)__ldg((const unsigned long long*)a.input_ids + off);
-}
 __device__ __forceinline__ int64_t raw_id(const MtrSamplerArgs& a, u64 raw) {
   return a.ids_dtype == MTR_IDS_I32 ? (int64_t)(int32_t)(uint32_t)raw : (int64_t)raw;
 }
@@ -2073,17 +2074,23 @@ __device__ __forceinline__ int32_t narrow_raw(const MtrSamplerArgs& a, u64 raw) 
 }
 
 // the previous token of the row ahead (lane 1; -1: none)
-__device__ __forceinline__ int64_t ahead_prev(const MtrSamplerArgs& a, const WarpAhead& w) {
-  if (w.s0 == RAW_NONE) return -1;
-  return (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) ? raw_id(a, w.s0) : (int64_t)(int32_t)(uint32_t)w.s0;
+// the last id of the row ahead, as int64 (-1 when the history is empty)
+__device__ __forceinline__ int64_t ahead_last(const MtrSamplerArgs& a, const WarpAhead& w, int L) {
+  if (L <= 0) return -1;
+  return a.ids_dtype == MTR_IDS_I32 ? (int64_t)(int32_t)w.last32 : (int64_t)w.last64;
+}
+// the previous token of the row ahead (lane 1; -1: none)
+__device__ __forceinline__ int64_t ahead_prev(const MtrSamplerArgs& a, const WarpAhead& w, int L) {
+  if (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) return ahead_last(a, w, L);
+  return a.prev_token ? (int64_t)w.prev : -1;
 }
 // second step of the row-ahead loads, issued once the first step has landed:
 // the class of the previous token (lane 1), so the row's prologue has no
 // dependent global load on the grammar path
-__device__ __forceinline__ void load_ahead_class(const MtrSamplerArgs& a, int lane, int V, WarpAhead& w) {
+__device__ __forceinline__ void load_ahead_class(const MtrSamplerArgs& a, int lane, int V, int L, WarpAhead& w) {
   w.cls = 0xffffffffu;
   if (lane == 1 && a.grammar_class_of) {
-    const int64_t prev = ahead_prev(a, w);
+    const int64_t prev = ahead_prev(a, w, L);
     if (prev >= 0 && prev < V) w.cls = __ldg(a.grammar_class_of + prev);
   }
 }
@@ -2107,29 +2114,26 @@ __device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derive
         if (32 * k < n) w.hid[k] = (u64)__ldg(p + 32 * k);
     }
   }
-  w.s0 = 0;
-  w.s1 = 0;
-  if (lane == 0) {
-    if (a.mono_mode == MTR_MONO_STATE) w.s0 = (u64)(uint32_t)a.mono_state[row];
-    if (L > 0 && (a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS)) w.s1 = load_raw_id(a, row, L - 1);
-  } else if (lane == 1) {
-    w.s0 = RAW_NONE;
-    if (a.grammar_class_of) {
-      if (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) {
-        if (L > 0) w.s0 = load_raw_id(a, row, L - 1);
-      } else if (a.prev_token) {
-        w.s0 = (u64)(uint32_t)a.prev_token[row];
-      }
-    }
-  } else if (lane == 3) {
-    if (a.select_mode == MTR_SELECT_SAMPLE) w.s1 = (u64)__float_as_uint(a.uniforms[row]);
+  const bool i32 = a.ids_dtype == MTR_IDS_I32;
+  const int64_t roff = row * a.ids_row_stride;
+  const bool need_last = L > 0 && ((lane == 0 && (a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS)) ||
+                                   (lane == 1 && a.grammar_class_of && (a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS)));
+  if (need_last) {
+    if (i32) w.last32 = __ldg((const uint32_t*)a.input_ids + roff + L - 1);
+    else w.last64 = __ldg((const unsigned long long*)a.input_ids + roff + L - 1);
   }
+  if (lane == 0 && a.mono_mode == MTR_MONO_STATE) w.mono = a.mono_state[row];
+  if (lane == 1 && a.grammar_class_of && !(a.flags & MTR_FLAG_GRAMMAR_PREV_FROM_IDS) && a.prev_token)
+    w.prev = a.prev_token[row];
+  if (lane == 3 && a.select_mode == MTR_SELECT_SAMPLE) w.ubits = __float_as_uint(a.uniforms[row]);
+  if (lane == 2 && a.temp_mode == MTR_TEMP_ROW_CONDITIONAL) {
 #pragma unroll
-  for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c) {
-    w.cond[c] = RAW_NONE;
-    if (lane == 2 && a.temp_mode == MTR_TEMP_ROW_CONDITIONAL && c < a.n_cond) {
+    for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c) {
       const int off = a.cond_offset[c];
-      if (off >= 1 && L >= off) w.cond[c] = load_raw_id(a, row, L - off);
+      if (c < a.n_cond && off >= 1 && L >= off) {
+        if (i32) w.cond32[c] = __ldg((const uint32_t*)a.input_ids + roff + L - off);
+        else w.cond64[c] = __ldg((const unsigned long long*)a.input_ids + roff + L - off);
+      }
     }
   }
 }
@@ -2189,7 +2193,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
   WarpAhead ah;
   if (row < a.num_rows) {
     load_ahead(a, dv, row, lane, L, ah);
-    load_ahead_class(a, lane, V, ah);
+    load_ahead_class(a, lane, V, L, ah);
   }
 
 #pragma unroll 1
@@ -2219,10 +2223,10 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       u64 gb = 0;
       float t = a.temperature, y = dv.temp_rcp, uu = 0.0f;
       if (lane == 0 && a.mono_mode == MTR_MONO_STATE) {
-        m0 = (int32_t)(uint32_t)ah.s0;
-        if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) m0 = mono_update(a, m0, raw_id(a, ah.s1));
+        m0 = ah.mono;
+        if ((a.flags & MTR_FLAG_MONO_UPDATE_FROM_IDS) && L > 0) m0 = mono_update(a, m0, ahead_last(a, ah, L));
       } else if (lane == 1 && a.grammar_class_of) {
-        const int64_t prev = ahead_prev(a, ah);
+        const int64_t prev = ahead_prev(a, ah, L);
         if (prev >= V) st |= MTR_ROW_BAD_ID;
         if (prev >= 0 && prev < V) {
           const uint32_t c = ah.cls;
@@ -2238,8 +2242,10 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         bool hit = false;  // first matching condition wins (static indices keep ah in registers)
 #pragma unroll
         for (int c = 0; c < MTR_MAX_COND_TEMPS; ++c) {
-          const int64_t tok = ah.cond[c] == RAW_NONE ? -1 : raw_id(a, ah.cond[c]);
-          if (!hit && c < a.n_cond && tok >= 0 && tok < V &&
+          const int off = a.cond_offset[c];
+          const bool have = c < a.n_cond && off >= 1 && L >= off;
+          const int64_t tok = !have ? -1 : (a.ids_dtype == MTR_IDS_I32 ? (int64_t)(int32_t)ah.cond32[c] : (int64_t)ah.cond64[c]);
+          if (!hit && have && tok >= 0 && tok < V &&
               ((__ldg(a.cond_token_bits[c] + (tok >> 5)) >> (tok & 31)) & 1u)) {
             t = a.cond_temperature[c];
             y = dv.cond_rcp[c];
@@ -2247,7 +2253,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           }
         }
       } else if (lane == 3 && sel == MTR_SELECT_SAMPLE) {
-        uu = __uint_as_float((uint32_t)ah.s1);
+        uu = __uint_as_float(ah.ubits);
         if (!(uu >= 0.0f)) {
           uu = 0.0f;
           st |= MTR_ROW_BAD_UNIFORM;
@@ -3341,7 +3347,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       if (a.mono_mode != MTR_MONO_OFF && a.mono_state) a.mono_state[row] = mm;
       if (a.out_status) a.out_status[row] = status;
     }
-    if (nrow < a.num_rows) load_ahead_class(a, lane, V, ah);  // the row-ahead values have landed by now
+    if (nrow < a.num_rows) load_ahead_class(a, lane, V, L, ah);  // the row-ahead values have landed by now
     __syncwarp();  // this row's readers of the shared regions are done
   }
 }
