@@ -2035,11 +2035,12 @@ __device__ __forceinline__ void sort64_desc(u64& a0, u64& a1, int lane) {
       const u64 p0 = __shfl_xor_sync(FULL, a0, j >> 1), p1 = __shfl_xor_sync(FULL, a1, j >> 1);
       const int g = 2 * lane;  // both positions share the bits k and j
       const bool keep_larger = ((g & k) == 0) == ((g & j) == 0);
-      a0 = keep_larger ? (p0 > a0 ? p0 : a0) : (p0 < a0 ? p0 : a0);
-      a1 = keep_larger ? (p1 > a1 ? p1 : a1) : (p1 < a1 ? p1 : a1);
+      // keys are distinct except the empty (zero) entries, where taking either is the same
+      if ((p0 > a0) == keep_larger) a0 = p0;
+      if ((p1 > a1) == keep_larger) a1 = p1;
     }
     const bool desc = ((2 * lane) & k) == 0;
-    const bool sw = desc ? a0 < a1 : a0 > a1;
+    const bool sw = (a0 < a1) == desc;
     const u64 t0 = sw ? a1 : a0, t1 = sw ? a0 : a1;
     a0 = t0;
     a1 = t1;
@@ -2337,11 +2338,12 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
 #pragma unroll
       for (int k = 0; k < WHIST; ++k) {
         const int pos = ah.hbase + lane + 32 * k;
-        const int32_t t = narrow_raw(a, ah.hid[k]);
         const bool in_window = pos >= a.penalty_start && pos < L;
-        const bool ok = in_window && t >= 0 && t < V;
+        // int32 ids are held zero-extended and RAW_NONE lies above every id,
+        // so one unsigned compare checks 0 <= id < V for both id types
+        const bool ok = in_window && ah.hid[k] < (u64)V;
         bad |= (uint32_t)(in_window && !ok);
-        ht[k] = ok ? t : -1;
+        ht[k] = ok ? (int32_t)ah.hid[k] : -1;
       }
       __syncwarp();
 #pragma unroll
@@ -2456,6 +2458,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
       if constexpr (SPLIT) {
         float* const Xlo = X + 4 * lane;
         float* const Xhi = X + HALF + 4 * lane;
+        u64 kcur = km[0];  // keep bits of slot s in the low byte
 #pragma unroll 2
         for (int s = 0; s < NS; ++s) {
           if ((s * 32 + lane) * 8 >= V) break;
@@ -2474,10 +2477,11 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
             for (int e = 0; e < 8; ++e) v[e] = E::get(ra, e);
           }
           if (masks) {
-            const uint32_t keep = (uint32_t)((s < 8 ? km[0] : km[1]) >> (8 * (s & 7)));
+            const uint32_t keep = (uint32_t)kcur;
 #pragma unroll
             for (int e = 0; e < 8; ++e) v[e] = ((keep >> e) & 1u) ? v[e] : NEG;
           }
+          kcur = s == 7 ? km[1] : kcur >> 8;
           *(float4*)(Xlo + 128 * s) = make_float4(v[0], v[1], v[2], v[3]);
           *(float4*)(Xhi + 128 * s) = make_float4(v[4], v[5], v[6], v[7]);
         }
@@ -2558,10 +2562,12 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         for (int h0 = 0; h0 < WHIST; h0 += WHIST / 2) {
           float xv[WHIST / 2];
           uint32_t cw[WHIST / 2];
+          int xo[WHIST / 2];
 #pragma unroll
           for (int k = 0; k < WHIST / 2; ++k) {
             const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
-            xv[k] = *xat(t);
+            xo[k] = SPLIT ? ((t & 4) ? HALF : 0) + ((t >> 3) << 2) + (t & 3) : t;  // float index of id t in X
+            xv[k] = X[xo[k]];
             cw[k] = cnt[t >> 1];
           }
           bool rare = false;
@@ -2588,7 +2594,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
           }
 #pragma unroll
           for (int k = 0; k < WHIST / 2; ++k)
-            if ((own >> (h0 + k)) & 1u) *xat(ht[h0 + k]) = xv[k];
+            if ((own >> (h0 + k)) & 1u) X[xo[k]] = xv[k];
         }
       } else {
         // long histories: owners are claimed through bit 15 of the counts (ids read again)
