@@ -1878,22 +1878,27 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
 // so chunk c's raw data sits exactly where its processed floats go.  fp32
 // logits: natural layout (id i at float i), the raw row copied in place.
 //
-// Dynamic shared memory per warp: X (VP floats) + a region that holds the u16
-// history counts during the chain and the selection state after it.
+// Dynamic shared memory per warp: X (VP floats) + a region that holds the
+// history counts during the chain and the selection state after it: 16 KB +
+// 5504 B at V = 4096, so ten warps fit on an SM (228 KB; per CTA 1 KB reserved,
+// 16 B static, 128 B granularity).
+// The counts are 8-bit; a row whose window repeats an id 256 times or more, or
+// whose penalty window reaches past the ids held in registers, is counted again
+// exactly with 16-bit counts over one half of the vocabulary at a time.
 // ---------------------------------------------------------------------------
 constexpr int WV_MAX = 4096;
 constexpr int WNB = 256;               // histogram bins
 constexpr float WBIN_SCALE = 8.0f;     // chunk-maximum bins per logit
-constexpr int WCAP = 256;              // candidate / survivor list
+constexpr int WCAP = 224;              // candidate / survivor list (a multiple of 32)
 constexpr int WMINI = 64;              // crossing-bin list
 constexpr int WHIST = 16;              // history ids per lane held in registers
-constexpr int WSEL_BYTES = WNB * 8 + WCAP * 12 + WMINI * 12 + 16;
+constexpr int WSEL_BYTES = WNB * 8 + WCAP * 12 + WMINI * 12;
 constexpr int WMAX_PEN_IDS = 32767;    // counts keep a claim bit in bit 15
 constexpr uint32_t WAIT_POLLS = 1u << 20;  // ~1 s of 1 us suspends before a copy counts as lost
 
 __host__ __device__ constexpr int warp_vpad(int V) { return (V + 255) / 256 * 256; }
 __host__ __device__ constexpr int warp_union_bytes(int V) {
-  return warp_vpad(V) * 2 > WSEL_BYTES ? warp_vpad(V) * 2 : WSEL_BYTES;
+  return warp_vpad(V) > WSEL_BYTES ? warp_vpad(V) : WSEL_BYTES;
 }
 __host__ __device__ constexpr int warp_bytes(int V) { return warp_vpad(V) * 4 + warp_union_bytes(V); }
 
@@ -2140,7 +2145,7 @@ __device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derive
 }
 
 template <typename Tin, bool CFG>
-__global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__ MtrSamplerArgs a,
+__global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant__ MtrSamplerArgs a,
                                                          const __grid_constant__ Derived dv) {
   using E = Elem<Tin>;
   constexpr int VEC = E::VEC;            // elements per 16-byte group
@@ -2156,7 +2161,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
   const int nch = (V + 7) / 8;
   float* X = (float*)dsm;
   uint8_t* U = dsm + (size_t)VP * 4;
-  uint32_t* cnt = (uint32_t*)U;          // chain: u16 history counts (bit 15 = claimed), two per word
+  uint32_t* cnt = (uint32_t*)U;          // chain: u8 history counts, four per word (exact path: u16, two per word)
   u64* hist = (u64*)U;                   // selection
   uint32_t* hc = (uint32_t*)U;
   float* lx = (float*)(U + WNB * 8);
@@ -2326,13 +2331,15 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
 
     // ---------------------------------------------------------- history counts
     uint32_t own = 0;  // bit k: this lane counted window id k first and applies its penalties
-    const bool long_hist = a.penalty_start < ah.hbase;  // ids outside the register window
+    // ids outside the register window, or an 8-bit count that wrapped: the exact
+    // 16-bit counts of the penalty step
+    bool exact_counts = a.penalty_start < ah.hbase;
     int32_t ht[WHIST];  // window ids inside the penalty window and [0, V), else -1
     if (dv.pen_on) {
 #pragma unroll
-      for (int i = 0; i < WV_MAX / 256; ++i) {
+      for (int i = 0; i < WV_MAX / 512; ++i) {
         const int w = (i * 32 + lane) * 4;
-        if (w < VP / 2) *(uint4*)(cnt + w) = make_uint4(0u, 0u, 0u, 0u);
+        if (w < VP / 4) *(uint4*)(cnt + w) = make_uint4(0u, 0u, 0u, 0u);
       }
       uint32_t bad = 0;
 #pragma unroll
@@ -2346,25 +2353,29 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         ht[k] = ok ? (int32_t)ah.hid[k] : -1;
       }
       __syncwarp();
+      uint32_t wrapped = 0;
 #pragma unroll
       for (int h0 = 0; h0 < WHIST; h0 += WHIST / 2) {
         uint32_t old[WHIST / 2];  // a half window of atomics in flight before any result is used
 #pragma unroll
         for (int k = 0; k < WHIST / 2; ++k) {
           old[k] = 0xffffffffu;
-          if (ht[h0 + k] >= 0) old[k] = atomicAdd(cnt + (ht[h0 + k] >> 1), 1u << (16 * (ht[h0 + k] & 1)));
+          if (ht[h0 + k] >= 0) old[k] = atomicAdd(cnt + (ht[h0 + k] >> 2), 1u << (8 * (ht[h0 + k] & 3)));
         }
 #pragma unroll
-        for (int k = 0; k < WHIST / 2; ++k)
-          own |= (uint32_t)(ht[h0 + k] >= 0 && ((old[k] >> (16 * (ht[h0 + k] & 1))) & 0xffffu) == 0u) << (h0 + k);
+        for (int k = 0; k < WHIST / 2; ++k) {
+          const uint32_t c = (old[k] >> (8 * (ht[h0 + k] & 3))) & 0xffu;
+          own |= (uint32_t)(ht[h0 + k] >= 0 && c == 0u) << (h0 + k);
+          wrapped |= (uint32_t)(ht[h0 + k] >= 0 && c == 0xffu);  // the add carried into the next id's count
+        }
       }
 #pragma unroll 1
-      for (int pos = a.penalty_start + lane; pos < ah.hbase; pos += 32) {  // long histories only
+      for (int pos = a.penalty_start + lane; pos < ah.hbase; pos += 32) {  // long histories: counted exactly later
         const int64_t t = load_id(a, row, pos);
         if (t < 0 || t >= V) bad = 1;
-        else atomicAdd(cnt + (t >> 1), 1u << (16 * (t & 1)));
       }
       if (__any_sync(FULL, bad)) status |= MTR_ROW_BAD_ID;
+      if (__any_sync(FULL, wrapped)) exact_counts = true;
       __syncwarp();
     }
 
@@ -2554,7 +2565,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
         float* p = xat(t);
         *p = pen_slow(*p, (float)count);
       };
-      if (!long_hist) {
+      if (!exact_counts) {
         // the lane that counted an id first applies it, with the final count;
         // per half of the window: loads first, then the arithmetic, then the stores
         const float y = dv.rep_rcp;
@@ -2568,13 +2579,13 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
             const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
             xo[k] = SPLIT ? ((t & 4) ? HALF : 0) + ((t >> 3) << 2) + (t & 3) : t;  // float index of id t in X
             xv[k] = X[xo[k]];
-            cw[k] = cnt[t >> 1];
+            cw[k] = cnt[t >> 2];
           }
           bool rare = false;
 #pragma unroll
           for (int k = 0; k < WHIST / 2; ++k) {
             const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
-            const float c = (float)((cw[k] >> (16 * (t & 1))) & 0xffffu);
+            const float c = (float)((cw[k] >> (8 * (t & 3))) & 0xffu);
             const float x = xv[k];
             const float ax = fabsf(x);
             // x / rp by Markstein for normal-range positive x; other operands go out of line
@@ -2589,7 +2600,7 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
 #pragma unroll
             for (int k = 0; k < WHIST / 2; ++k) {
               const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
-              xv[k] = pen_slow(*xat(t), (float)((cnt[t >> 1] >> (16 * (t & 1))) & 0xffffu));
+              xv[k] = pen_slow(*xat(t), (float)((cnt[t >> 2] >> (8 * (t & 3))) & 0xffu));
             }
           }
 #pragma unroll
@@ -2597,16 +2608,31 @@ __global__ void __launch_bounds__(32, 9) row_warp_kernel(const __grid_constant__
             if ((own >> (h0 + k)) & 1u) X[xo[k]] = xv[k];
         }
       } else {
-        // long histories: owners are claimed through bit 15 of the counts (ids read again)
-        auto claim = [&](int32_t t) {
-          const uint32_t sh = 16u * (uint32_t)(t & 1);
-          const uint32_t old = atomicOr(cnt + (t >> 1), 0x8000u << sh);
-          if (!((old >> sh) & 0x8000u)) pen(t, (old >> sh) & 0x7fffu);
-        };
+        // exact counts: 16 bits per id over one half of the vocabulary at a time
+        // (the ids read again); bit 15 claims an id for the lane that applies it
+        const int H = VP / 2;
 #pragma unroll 1
-        for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
-          const int64_t t = load_id(a, row, pos);
-          if (t >= 0 && t < V) claim((int32_t)t);
+        for (int lo = 0; lo < VP; lo += H) {
+          __syncwarp();
+#pragma unroll 1
+          for (int w = lane * 4; w < H / 2; w += 128) *(uint4*)(cnt + w) = make_uint4(0u, 0u, 0u, 0u);
+          __syncwarp();
+#pragma unroll 1
+          for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
+            const int64_t t = load_id(a, row, pos);
+            if (t >= lo && t < lo + H && t < V) atomicAdd(cnt + ((t - lo) >> 1), 1u << (16 * ((t - lo) & 1)));
+          }
+          __syncwarp();
+#pragma unroll 1
+          for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
+            const int64_t t = load_id(a, row, pos);
+            if (t >= lo && t < lo + H && t < V) {
+              const int r = (int)(t - lo);
+              const uint32_t sh = 16u * (uint32_t)(r & 1);
+              const uint32_t old = atomicOr(cnt + (r >> 1), 0x8000u << sh);
+              if (!((old >> sh) & 0x8000u)) pen((int32_t)t, (old >> sh) & 0x7fffu);
+            }
+          }
         }
       }
       __syncwarp();
@@ -3686,7 +3712,7 @@ int mtr_sampler_query_args(const MtrSamplerArgs* a, MtrLaunchInfo* out) {
             cudaSuccess ||
         occ < 1) {
       cudaGetLastError();
-      occ = 9;  // no device: the launch bound
+      occ = 10;  // no device: the launch bound
     }
     const int64_t cap = (int64_t)occ * sms;
     out->grid = (int32_t)(a->num_rows < cap ? a->num_rows : cap);

@@ -359,3 +359,29 @@ def test_penalties_then_temperature(cuda_device, temp):
                      frequency_penalty=0.2, presence_penalty=0.1, select_mode=N.SELECT_SAMPLE, top_k=50, top_p=0.95,
                      uniforms=rng.random(rows, dtype=np.float32), want_scores=True, **kw)
     assert_parity(s, cuda_device)
+
+
+@pytest.mark.parametrize("ids_dtype", [np.int64, np.int32])
+def test_repeated_ids_count_wrap(cuda_device, ids_dtype):
+    # one id repeated 255, 256, 300 and 511 times inside a 512-id window, next to
+    # its neighbour ids: the row-per-warp kernel's 8-bit counts wrap from the
+    # 256th repeat on and the row is counted again exactly
+    rng = np.random.default_rng(151)
+    rows, V, L = 320, 4096, 512
+    x = W.bf16_bits(rng.normal(0, 2, size=(rows, V)).astype(np.float32))
+    for start in (0, 100):
+        ids = rng.integers(0, V, size=(rows, L)).astype(ids_dtype)
+        for r in range(rows):
+            reps = (255, 256, 300, 511)[r % 4]
+            h = int(rng.integers(1, V - 1))
+            pos = rng.permutation(L)
+            ids[r, pos[:reps]] = h
+            if reps < L:
+                ids[r, pos[reps:reps + 1]] = h + 1
+            if reps + 1 < L:
+                ids[r, pos[reps + 1:reps + 2]] = h - 1
+        s = W.StepInputs(logits=x, dtype="bf16", num_rows=rows, input_ids=ids, penalty_start=start,
+                         repetition_penalty=1.2, frequency_penalty=0.01, presence_penalty=0.05,
+                         select_mode=N.SELECT_SAMPLE, top_k=40, top_p=0.9,
+                         uniforms=rng.random(rows, dtype=np.float32), want_scores=True)
+        assert_parity(s, cuda_device)
