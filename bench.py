@@ -62,6 +62,9 @@ def parse_args():
     p.add_argument("--profile", type=int, default=0,
                    help="only run this many eager launches of one workload (for ncu), print nothing")
     p.add_argument("--profile-workload", choices=["sharded", "b64"], default="sharded")
+    p.add_argument("--sweep", action="store_true",
+                   help="instead of the headline line: one line per vocabulary-sweep workload (rows x V bf16, "
+                        "penalties + top_k 50 + top_p 0.95), device-timed, with its HBM roofline")
     return p.parse_args()
 
 
@@ -450,11 +453,67 @@ def run_reference(args, dist: Dist):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- vocabulary sweep
+SWEEP = ((256, 4096), (256, 16384), (256, 65536), (1024, 4096))
+
+
+def run_sweep(args, dist):
+    """rows x V bf16 logits N(0, 2^2), 512-id int64 history uniform over V, repetition 1.1 / frequency 0.2 /
+    presence 0.1, top_k 50, top_p 0.95, inverse-CDF draw; no CFG.  One line per (rows, V)."""
+    from mapperatorinator_b200 import _native
+    from mapperatorinator_b200.sampling import FusedSampler
+
+    _native.load()  # fail loudly without the native library
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.Stream(device)
+    peak, peak_kind = measured_peak()
+    for rows, vocab in SWEEP:
+        gen = torch.Generator(device).manual_seed(4321 + rows + vocab)
+        s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, repetition_penalty=1.1,
+                         frequency_penalty=0.2, presence_penalty=0.1, top_k=50, top_p=0.95)
+        hist = torch.randint(0, vocab, (rows, HISTORY), generator=gen, device=device)
+        buf_bytes = rows * vocab * 2
+        nbuf = max(4, math.ceil(3 * L2_BYTES / buf_bytes))
+        pool = [(torch.randn((rows, vocab), generator=gen, device=device) * 2.0).to(torch.bfloat16)
+                for _ in range(nbuf)]
+        upool = torch.rand((nbuf, rows), generator=gen, device=device)
+
+        def step(i, s=s, pool=pool, upool=upool, hist=hist, nbuf=nbuf):
+            s.step(pool[i % nbuf], hist, uniforms=upool[i % nbuf])
+
+        with torch.cuda.stream(stream):
+            for i in range(max(3, args.warmup)):
+                step(i)
+        torch.cuda.synchronize()
+        info = s.launch_info(pool[0], hist, upool[0])
+        steps = max(64, min(args.steps, 2048))
+        ms, graph = time_graph(step, steps, stream, dist)
+        ms = dist.max(ms)
+        del graph
+        us = ms * 1e3 / steps
+        nbytes = rows * vocab * 2 + rows * HISTORY * 8 + rows * (4 + 8 + 4)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        kernel = "mtr::row_warp_kernel" if info.kernel == _native.KERNEL_ROW_WARP else "mtr::sampler_kernel"
+        if dist.rank == 0:
+            print(json.dumps({"workload": "vocab_sweep", "rows": rows, "vocab": vocab, "rows_x_vocab": rows * vocab,
+                              "us_per_step": us, "tokens_per_s": rows / (us * 1e-6), "steps": steps,
+                              "algorithmic_bytes_per_launch": nbytes, "achieved_gbs": gbs, "peak_gbs": peak,
+                              "frac": gbs / peak, "peak_kind": peak_kind, "kernel": kernel, "grid": info.grid,
+                              "threads": info.threads, "cluster": info.cluster_size,
+                              "l2": f"logits rotate over {nbuf} buffers ({nbuf * buf_bytes / 2**20:.0f} MiB)"}),
+                  flush=True)
+        del s, pool, upool, hist
+        torch.cuda.empty_cache()
+
+
 def main():
     args = parse_args()
     dist = Dist()
     try:
-        if args.impl == "reference":
+        if args.sweep:
+            run_sweep(args, dist)
+        elif args.impl == "reference":
             run_reference(args, dist)
         else:
             run_ours(args, dist)
