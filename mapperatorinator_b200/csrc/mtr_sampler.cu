@@ -1684,79 +1684,120 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
             for (int e = 0; e < VEC; ++e) s += q[j * VEC + e];
             cs[j] = s;
           }
-          Clu<CS>::sync();  // wl / cta_mass free for reuse
-#pragma unroll
-          for (int j = 0; j < NCH; ++j) {
-            const u64 s = warp_sum_u64(cs[j]);
-            if (lane == 0) sm.wl[j * 32 + warp] = s;
-          }
-          __syncthreads();
-          u64 ctot[NCH];
-          u64 cta = 0;
-#pragma unroll
-          for (int j = 0; j < NCH; ++j) {
-            u64 s = 0;
-            for (int w = 0; w < NW; ++w) s += sm.wl[j * 32 + w];
-            ctot[j] = s;
-            cta += s;
-          }
-          if (tid == 0) sm.cta_mass = cta;
-          Clu<CS>::sync();
-          // which CTA holds the draw (R < qkept = sum of the CTA masses)
-          u64 before = 0;
-          int cstar = -1;
-#pragma unroll
-          for (int r = 0; r < CS; ++r) {
-            const u64 m = *Clu<CS>::at(&sm.cta_mass, r);
-            if (cstar < 0) {
-              if (R < before + m) cstar = r;
-              else before += m;
-            }
-          }
-          if (cstar < 0) cstar = CS - 1;
-          owner = cstar;
-          if (crank == cstar) {
-            u64 rr = R - before;
-            int jstar = -1;
+          if constexpr (CS == 1) {
+            // ids run chunk-major (chunk j of every thread, then chunk j + 1), so one
+            // warp scan per chunk and the warp totals locate the thread and chunk
+            // holding the draw without forming the CTA total first
+            if (tid == 0) sm.token = 0;
+            __syncthreads();  // wl free for reuse
+            u64 inc[NCH];
 #pragma unroll
             for (int j = 0; j < NCH; ++j) {
-              if (jstar < 0) {
-                if (rr < ctot[j]) jstar = j;
-                else rr -= ctot[j];
-              }
+              inc[j] = warp_incl_scan_u64(cs[j], lane);
+              if (lane == 31) sm.wl[j * 32 + warp] = inc[j];
             }
-            if (jstar < 0) jstar = NCH - 1;
-            u64 mine = 0;
-#pragma unroll
-            for (int j = 0; j < NCH; ++j)
-              if (j == jstar) mine = cs[j];
-            // exclusive scan of `mine` over the CTA
-            const u64 incl = warp_incl_scan_u64(mine, lane);
-            if (lane == 31) sm.wl[warp] = incl;
             __syncthreads();
-            u64 wbefore = 0;
-            for (int w = 0; w < warp; ++w) wbefore += sm.wl[w];
-            const u64 excl = wbefore + incl - mine;
-            if (mine != 0 && excl <= rr && rr < excl + mine) {
-              u64 c = excl;
-              bool found = false;
+            u64 chunk_base = 0;
 #pragma unroll
-              for (int j = 0; j < NCH; ++j) {
+            for (int j = 0; j < NCH; ++j) {
+              u64 wb = 0, wt = 0;
+              for (int w = 0; w < NW; ++w) {
+                const u64 v = sm.wl[j * 32 + w];
+                wb += w < warp ? v : 0ull;
+                wt += v;
+              }
+              const u64 lo = chunk_base + wb + inc[j] - cs[j];
+              if (cs[j] != 0 && lo <= R && R < lo + cs[j]) {
+                u64 c = lo;
+                bool found = false;
 #pragma unroll
                 for (int e = 0; e < VEC; ++e) {
-                  const int k = j * VEC + e;
-                  if (j == jstar && !found) {
-                    c += q[k];
-                    if (c > rr) {
-                      sm.token = id_of(k);
-                      found = true;
+                  c += q[j * VEC + e];
+                  if (!found && c > R) {
+                    sm.token = id_of(j * VEC + e);
+                    found = true;
+                  }
+                }
+              }
+              chunk_base += wt;
+            }
+            __syncthreads();
+            token = sm.token;
+          } else {
+            Clu<CS>::sync();  // wl / cta_mass free for reuse
+  #pragma unroll
+            for (int j = 0; j < NCH; ++j) {
+              const u64 s = warp_sum_u64(cs[j]);
+              if (lane == 0) sm.wl[j * 32 + warp] = s;
+            }
+            __syncthreads();
+            u64 ctot[NCH];
+            u64 cta = 0;
+  #pragma unroll
+            for (int j = 0; j < NCH; ++j) {
+              u64 s = 0;
+              for (int w = 0; w < NW; ++w) s += sm.wl[j * 32 + w];
+              ctot[j] = s;
+              cta += s;
+            }
+            if (tid == 0) sm.cta_mass = cta;
+            Clu<CS>::sync();
+            // which CTA holds the draw (R < qkept = sum of the CTA masses)
+            u64 before = 0;
+            int cstar = -1;
+  #pragma unroll
+            for (int r = 0; r < CS; ++r) {
+              const u64 m = *Clu<CS>::at(&sm.cta_mass, r);
+              if (cstar < 0) {
+                if (R < before + m) cstar = r;
+                else before += m;
+              }
+            }
+            if (cstar < 0) cstar = CS - 1;
+            owner = cstar;
+            if (crank == cstar) {
+              u64 rr = R - before;
+              int jstar = -1;
+  #pragma unroll
+              for (int j = 0; j < NCH; ++j) {
+                if (jstar < 0) {
+                  if (rr < ctot[j]) jstar = j;
+                  else rr -= ctot[j];
+                }
+              }
+              if (jstar < 0) jstar = NCH - 1;
+              u64 mine = 0;
+  #pragma unroll
+              for (int j = 0; j < NCH; ++j)
+                if (j == jstar) mine = cs[j];
+              // exclusive scan of `mine` over the CTA
+              const u64 incl = warp_incl_scan_u64(mine, lane);
+              if (lane == 31) sm.wl[warp] = incl;
+              __syncthreads();
+              u64 wbefore = 0;
+              for (int w = 0; w < warp; ++w) wbefore += sm.wl[w];
+              const u64 excl = wbefore + incl - mine;
+              if (mine != 0 && excl <= rr && rr < excl + mine) {
+                u64 c = excl;
+                bool found = false;
+  #pragma unroll
+                for (int j = 0; j < NCH; ++j) {
+  #pragma unroll
+                  for (int e = 0; e < VEC; ++e) {
+                    const int k = j * VEC + e;
+                    if (j == jstar && !found) {
+                      c += q[k];
+                      if (c > rr) {
+                        sm.token = id_of(k);
+                        found = true;
+                      }
                     }
                   }
                 }
               }
+              __syncthreads();
+              token = sm.token;
             }
-            __syncthreads();
-            token = sm.token;
           }
         }
       }
