@@ -2092,6 +2092,68 @@ __device__ __forceinline__ void sort64_desc(u64& a0, u64& a1, int lane) {
     a1 = t1;
   }
 }
+// repetition (x < 0 ? x * rp : x / rp), then frequency and presence, each step
+// skipped when it is the identity (rp = 1, fp = 0, pp = 0); y = RN(1 / rp) or 0
+__device__ __forceinline__ float pen_value(float x, float c, float rp, float fp, float pp, float y) {
+  if (rp != 1.0f) x = x < 0.0f ? __fmul_rn(x, rp) : (y != 0.0f ? div_by(x, rp, y) : div_rare(x, rp));
+  if (fp != 0.0f) x = __fsub_rn(x, __fmul_rn(fp, c));
+  if (pp != 0.0f) x = __fsub_rn(x, pp);
+  return x;
+}
+// Penalties of up to eight owned window ids (bit k of own8: id ids.t[k]) with
+// the IEEE divide for rare operands (zero, tiny, huge or NaN scores, or a
+// repetition penalty outside the fast divide's range): the same steps as the
+// common loop, out of line so that loop stays short.
+struct PenIds8 {
+  int32_t t[8];
+};
+__device__ __noinline__ void pen_rare8(float* X, const uint32_t* cnt, const PenIds8 ids, uint32_t own8, int half,
+                                       bool split, float rp, float fp, float pp, float y) {
+#pragma unroll 1
+  for (int k = 0; k < 8; ++k) {
+    if (!((own8 >> k) & 1u)) continue;
+    const int t = ids.t[k];
+    const int xo = split ? ((t & 4) ? half : 0) + ((t >> 3) << 2) + (t & 3) : t;
+    const float c = (float)((cnt[t >> 2] >> (8 * (t & 3))) & 0xffu);
+    X[xo] = pen_value(X[xo], c, rp, fp, pp, y);
+  }
+}
+// Penalties from exact 16-bit counts, for rows whose penalty window reaches
+// past the ids held in registers or repeats an id 256 times or more: one half
+// of the vocabulary at a time, the ids read again, bit 15 of a count claiming
+// the id for the lane that applies it.  Out of line: rare rows only.
+__device__ __noinline__ void pen_exact(float* X, uint32_t* cnt, const MtrSamplerArgs& a, int64_t row, int L, int V,
+                                       int VP, bool split, int lane, float rp, float fp, float pp, float y) {
+  const int H = VP / 2;
+#pragma unroll 1
+  for (int lo = 0; lo < VP; lo += H) {
+    __syncwarp();
+#pragma unroll 1
+    for (int w = lane * 4; w < H / 2; w += 128) *(uint4*)(cnt + w) = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
+#pragma unroll 1
+    for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
+      const int64_t t = load_id(a, row, pos);
+      if (t >= lo && t < lo + H && t < V) atomicAdd(cnt + ((t - lo) >> 1), 1u << (16 * ((t - lo) & 1)));
+    }
+    __syncwarp();
+#pragma unroll 1
+    for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
+      const int64_t t = load_id(a, row, pos);
+      if (t >= lo && t < lo + H && t < V) {
+        const int r = (int)(t - lo);
+        const uint32_t sh = 16u * (uint32_t)(r & 1);
+        const uint32_t old = atomicOr(cnt + (r >> 1), 0x8000u << sh);
+        if (!((old >> sh) & 0x8000u)) {
+          const int ti = (int)t;
+          const int xo = split ? ((ti & 4) ? H : 0) + ((ti >> 3) << 2) + (ti & 3) : ti;
+          X[xo] = pen_value(X[xo], (float)((old >> sh) & 0x7fffu), rp, fp, pp, y);
+        }
+      }
+    }
+  }
+  __syncwarp();
+}
 // per-row values loaded one row ahead.  Loads only: every value stays raw
 // (no arithmetic on a loaded register) until the row that uses it, so issuing
 // them never waits on memory.
@@ -2595,17 +2657,8 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
       __syncwarp();
       const float rp = a.repetition_penalty, fp = a.frequency_penalty, pp = a.presence_penalty;
       // repetition (x < 0 ? x * rp : x / rp), then frequency and presence; with
-      // rp = 1, fp = 0 or pp = 0 the step is the identity, so no step is skipped
-      auto pen_slow = [&](float x, float c) -> float {
-        if (rp != 1.0f) x = x < 0.0f ? __fmul_rn(x, rp) : (dv.rep_rcp != 0.0f ? div_by(x, rp, dv.rep_rcp) : div_rare(x, rp));
-        if (fp != 0.0f) x = __fsub_rn(x, __fmul_rn(fp, c));
-        if (pp != 0.0f) x = __fsub_rn(x, pp);
-        return x;
-      };
-      auto pen = [&](int32_t t, uint32_t count) {
-        float* p = xat(t);
-        *p = pen_slow(*p, (float)count);
-      };
+      // rp = 1, fp = 0 or pp = 0 the step is the identity, so the common loop
+      // skips none (pen_value, used out of line, skips them)
       if (!exact_counts) {
         // the lane that counted an id first applies it, with the final count;
         // per half of the window: loads first, then the arithmetic, then the stores
@@ -2638,43 +2691,18 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
             xv[k] = __fsub_rn(r, pp);
           }
           if (__any_sync(FULL, rare)) {
+            PenIds8 ids;
 #pragma unroll
-            for (int k = 0; k < WHIST / 2; ++k) {
-              const int32_t t = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
-              xv[k] = pen_slow(*xat(t), (float)((cnt[t >> 2] >> (8 * (t & 3))) & 0xffu));
-            }
+            for (int k = 0; k < WHIST / 2; ++k) ids.t[k] = ((own >> (h0 + k)) & 1u) ? ht[h0 + k] : 0;
+            pen_rare8(X, cnt, ids, (own >> h0) & 0xffu, HALF, SPLIT, rp, fp, pp, dv.rep_rcp);
+          } else {
+#pragma unroll
+            for (int k = 0; k < WHIST / 2; ++k)
+              if ((own >> (h0 + k)) & 1u) X[xo[k]] = xv[k];
           }
-#pragma unroll
-          for (int k = 0; k < WHIST / 2; ++k)
-            if ((own >> (h0 + k)) & 1u) X[xo[k]] = xv[k];
         }
       } else {
-        // exact counts: 16 bits per id over one half of the vocabulary at a time
-        // (the ids read again); bit 15 claims an id for the lane that applies it
-        const int H = VP / 2;
-#pragma unroll 1
-        for (int lo = 0; lo < VP; lo += H) {
-          __syncwarp();
-#pragma unroll 1
-          for (int w = lane * 4; w < H / 2; w += 128) *(uint4*)(cnt + w) = make_uint4(0u, 0u, 0u, 0u);
-          __syncwarp();
-#pragma unroll 1
-          for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
-            const int64_t t = load_id(a, row, pos);
-            if (t >= lo && t < lo + H && t < V) atomicAdd(cnt + ((t - lo) >> 1), 1u << (16 * ((t - lo) & 1)));
-          }
-          __syncwarp();
-#pragma unroll 1
-          for (int pos = a.penalty_start + lane; pos < L; pos += 32) {
-            const int64_t t = load_id(a, row, pos);
-            if (t >= lo && t < lo + H && t < V) {
-              const int r = (int)(t - lo);
-              const uint32_t sh = 16u * (uint32_t)(r & 1);
-              const uint32_t old = atomicOr(cnt + (r >> 1), 0x8000u << sh);
-              if (!((old >> sh) & 0x8000u)) pen((int32_t)t, (old >> sh) & 0x7fffu);
-            }
-          }
-        }
+        pen_exact(X, cnt, a, row, L, V, VP, SPLIT, lane, rp, fp, pp, dv.rep_rcp);
       }
       __syncwarp();
       if (pen_temp) {
@@ -3074,25 +3102,49 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
           if (pcut + 1 < 64 && nk != 0ull && (uint32_t)(nk >> 32) == (uint32_t)(ck >> 32)) status |= MTR_ROW_TIE_AT_CUT;
         }
         if (sel == MTR_SELECT_SAMPLE) {
-          // the smallest id whose id-ordered kept mass exceeds R, by binary search
-          // over ids (the kept mass only grows at kept ids)
+          // the smallest id whose id-ordered kept mass exceeds R: the kept mass of
+          // 32 id buckets (low and high 16 bits of q summed apart, so the shared
+          // atomics are 32-bit), a warp scan for the bucket where the mass crosses
+          // R, then the few kept entries inside that bucket
           const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
           const bool kp0 = q0 != 0u && j0 <= pcut, kp1 = q1 != 0u && j1 <= pcut;
           const int i0 = (int)(~(uint32_t)a0), i1 = (int)(~(uint32_t)a1);
-          auto mass_le = [&](int m) -> u64 {  // kept mass of ids <= m (q < 2^31, <= 64 terms)
-            const uint32_t c0 = (kp0 && i0 <= m) ? q0 : 0u, c1 = (kp1 && i1 <= m) ? q1 : 0u;
-            const uint32_t lo16 = __reduce_add_sync(FULL, (c0 & 0xffffu) + (c1 & 0xffffu));
-            const uint32_t hi16 = __reduce_add_sync(FULL, (c0 >> 16) + (c1 >> 16));
-            return ((u64)hi16 << 16) + lo16;
-          };
-          int lo = 0, hi = V - 1;  // mass_le(V - 1) = qkept > R
-#pragma unroll 1
-          while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (mass_le(mid) > R) hi = mid;
-            else lo = mid + 1;
+          int bsh = 3;  // bucket width 2^bsh: 32 buckets cover [0, VP)
+          while ((32 << bsh) < VP) ++bsh;
+          uint32_t* const bk = hc;  // bucket b: low-half sum at bk[2b], high-half sum at bk[2b + 1]
+          *(uint2*)(bk + 2 * lane) = make_uint2(0u, 0u);
+          __syncwarp();
+          if (kp0) {
+            atomicAdd(bk + 2 * (i0 >> bsh), q0 & 0xffffu);
+            atomicAdd(bk + 2 * (i0 >> bsh) + 1, q0 >> 16);
           }
-          token = lo;
+          if (kp1) {
+            atomicAdd(bk + 2 * (i1 >> bsh), q1 & 0xffffu);
+            atomicAdd(bk + 2 * (i1 >> bsh) + 1, q1 >> 16);
+          }
+          __syncwarp();
+          const uint2 hh = *(const uint2*)(bk + 2 * lane);
+          const u64 hb = ((u64)hh.y << 16) + hh.x;
+          const u64 incl = warp_incl_scan_u64(hb, lane);
+          const int b = max(__ffs(__ballot_sync(FULL, incl > R)) - 1, 0);  // the total qkept exceeds R
+          u64 f0 = __shfl_sync(FULL, incl - hb, b), f1 = f0;
+          const bool in0 = kp0 && (i0 >> bsh) == b, in1 = kp1 && (i1 >> bsh) == b;
+          unsigned m0 = __ballot_sync(FULL, in0), m1 = __ballot_sync(FULL, in1);
+#pragma unroll 1
+          while (m0 | m1) {  // each entry of the bucket adds its mass to the entries at or above its id
+            const bool from0 = m0 != 0u;
+            const int src = __ffs(from0 ? m0 : m1) - 1;
+            if (from0) m0 &= m0 - 1u;
+            else m1 &= m1 - 1u;
+            const int is = __shfl_sync(FULL, from0 ? i0 : i1, src);
+            const uint32_t qs = __shfl_sync(FULL, from0 ? q0 : q1, src);
+            f0 += is <= i0 ? qs : 0u;
+            f1 += is <= i1 ? qs : 0u;
+          }
+          int32_t my = NO_ID;
+          if (in0 && f0 > R && f0 - q0 <= R) my = i0;
+          if (in1 && f1 > R && f1 - q1 <= R) my = i1;
+          token = __reduce_min_sync(FULL, my);
         }
       }
     } else     if (need_mass && n >= 0) {
