@@ -2028,6 +2028,45 @@ __device__ __forceinline__ int warp_crossing(const W* h, u64 lim, int lane, u64&
   return __shfl_sync(FULL, my_b, src);
 }
 
+// warp_crossing over a histogram kept as low / high 16-bit sums of its weights
+// (bin i weighs lo[i] + hi[i] * 2^16), so its updates are 32-bit shared atomics
+__device__ __forceinline__ int warp_crossing_halves(const uint32_t* lo, const uint32_t* hi, u64 lim, int lane,
+                                                    u64& above, u64& w) {
+  u64 v[8];
+  {
+    const uint4 l0 = *(const uint4*)(lo + lane * 8), l1 = *(const uint4*)(lo + lane * 8 + 4);
+    const uint4 h0 = *(const uint4*)(hi + lane * 8), h1 = *(const uint4*)(hi + lane * 8 + 4);
+    v[0] = l0.x + ((u64)h0.x << 16); v[1] = l0.y + ((u64)h0.y << 16);
+    v[2] = l0.z + ((u64)h0.z << 16); v[3] = l0.w + ((u64)h0.w << 16);
+    v[4] = l1.x + ((u64)h1.x << 16); v[5] = l1.y + ((u64)h1.y << 16);
+    v[6] = l1.z + ((u64)h1.z << 16); v[7] = l1.w + ((u64)h1.w << 16);
+  }
+  u64 s = 0;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) s += v[r];
+  const u64 incl = warp_incl_scan_u64(s, lane);
+  int my_b = -1;
+  u64 my_above = 0, my_w = 0;
+  if (incl - s <= lim && lim < incl) {
+    u64 c = incl - s;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (my_b < 0 && c + v[r] > lim) {
+        my_b = lane * 8 + r;
+        my_above = c;
+        my_w = v[r];
+      }
+      c += v[r];
+    }
+  }
+  const unsigned bal = __ballot_sync(FULL, my_b >= 0);
+  if (!bal) return -1;
+  const int src = __ffs(bal) - 1;
+  above = __shfl_sync(FULL, my_above, src);
+  w = __shfl_sync(FULL, my_w, src);
+  return __shfl_sync(FULL, my_b, src);
+}
+
 // a chunk that a column-range edge splits: element by element (out of line)
 __device__ __noinline__ void temp_chunk_split(const MtrSamplerArgs& a, const Derived& dv, float (&v)[8], int id0) {
   for (int e = 0; e < 8; ++e) {
@@ -3174,12 +3213,18 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
 #pragma unroll 1
         for (int i = lane * 2; i < WNB; i += 64) *(ulonglong2*)(hist + i) = make_ulonglong2(0ull, 0ull);
         __syncwarp();
+        uint32_t* const hlo = (uint32_t*)hist;  // the 256 u64 bins as 256 low-half and 256 high-half sums
+        uint32_t* const hhi = hlo + WNB;
 #pragma unroll 1
         for (int j = lane; j < n; j += 32)
-          if (lq[j]) atomicAdd(hist + dbin3(lx[j]), (u64)lq[j]);
+          if (lq[j]) {
+            const int b = dbin3(lx[j]);
+            atomicAdd(hlo + b, lq[j] & 0xffffu);
+            atomicAdd(hhi + b, lq[j] >> 16);
+          }
         __syncwarp();
         u64 above3, w3;
-        const int b3 = max(warp_crossing(hist, plim, lane, above3, w3), 0);  // plim < total
+        const int b3 = max(warp_crossing_halves(hlo, hhi, plim, lane, above3, w3), 0);  // plim < total
         // canonical order (score desc, id asc) inside the crossing bin
         int m = 0;
 #pragma unroll 1
@@ -3257,12 +3302,17 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
         auto kept = [&](int j) -> bool {
           return lq[j] != 0u && (!topp_cut || lx[j] > cut_x || (lx[j] == cut_x && lid[j] <= cut_id));
         };
+        uint32_t* const hlo = (uint32_t*)hist;  // low / high 16-bit sums, as above
+        uint32_t* const hhi = hlo + WNB;
 #pragma unroll 1
         for (int j = lane; j < n; j += 32)
-          if (kept(j)) atomicAdd(hist + (lid[j] >> ish), (u64)lq[j]);
+          if (kept(j)) {
+            atomicAdd(hlo + (lid[j] >> ish), lq[j] & 0xffffu);
+            atomicAdd(hhi + (lid[j] >> ish), lq[j] >> 16);
+          }
         __syncwarp();
         u64 above4, w4;
-        const int b4 = max(warp_crossing(hist, R, lane, above4, w4), 0);  // R < qkept
+        const int b4 = max(warp_crossing_halves(hlo, hhi, R, lane, above4, w4), 0);  // R < qkept
         int m = 0;
 #pragma unroll 1
         for (int j0 = 0; j0 < n; j0 += 32) {
