@@ -2337,12 +2337,12 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
   __syncwarp();
   int64_t row = blockIdx.x;
   uint32_t parity = 0;
-  if (bulk && lane == 0 && row < a.num_rows) issue_copy(row);
+  // the first row's history ids and per-row values go out before its logits:
+  // the counts and masks need them first and can then run while the logits land
   WarpAhead ah;
-  if (row < a.num_rows) {
-    load_ahead(a, dv, row, lane, L, ah);
-    load_ahead_class(a, lane, V, L, ah);
-  }
+  if (row < a.num_rows) load_ahead(a, dv, row, lane, L, ah);
+  if (bulk && lane == 0 && row < a.num_rows) issue_copy(row);
+  if (row < a.num_rows) load_ahead_class(a, lane, V, L, ah);
 
 #pragma unroll 1
   for (; row < a.num_rows; row += gridDim.x) {
