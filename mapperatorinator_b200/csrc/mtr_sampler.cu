@@ -652,6 +652,30 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   auto chunk_id = [&](int j) -> int { return base + (j * THREADS + tid) * VEC; };
 
   // ------------------------------------------------------------ prologue
+  // this CTA's logits and first history ids are requested before the prologue's
+  // dependent-load chains, so their latency overlaps the chains' instead of
+  // following it on the warps that run a chain
+  const Tin* r1 = (const Tin*)a.logits + row * a.logits_row_stride;
+  const Tin* r2 = r1 + dv.second * a.logits_row_stride;
+  uint4 ra[NCH], rb[NCH];
+  if (dv.vec_ok) {
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) {
+      const int id0 = chunk_id(j);
+      ra[j] = make_uint4(0u, 0u, 0u, 0u);
+      rb[j] = make_uint4(0u, 0u, 0u, 0u);
+      if (id0 < V) {
+        ra[j] = __ldcs((const uint4*)(r1 + id0));
+        if (a.cfg_enabled) rb[j] = __ldcs((const uint4*)(r2 + id0));
+      }
+    }
+  }
+  int64_t hist0 = -1, hist1 = -1;  // first history ids of the penalty window
+  if (dv.pen_on) {
+    const int i0 = a.penalty_start + tid, i1 = i0 + THREADS;
+    if (i0 < L) hist0 = load_id(a, row, i0);
+    if (i1 < L) hist1 = load_id(a, row, i1);
+  }
   for (int i = tid; i < NB; i += THREADS) sm.hcnt[i] = 0u;
   int32_t mono = -1;
   if (a.mono_mode == MTR_MONO_SCAN) {
@@ -756,30 +780,10 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       sm.token = -1;
     }
   }
-  // first history ids of the penalty window, fetched before the barrier
-  int64_t hist0 = -1, hist1 = -1;
-  if (dv.pen_on) {
-    const int i0 = a.penalty_start + tid, i1 = i0 + THREADS;
-    if (i0 < L) hist0 = load_id(a, row, i0);
-    if (i1 < L) hist1 = load_id(a, row, i1);
-  }
 
   // ------------------------------------------------------------ load (+ CFG)
-  const Tin* r1 = (const Tin*)a.logits + row * a.logits_row_stride;
-  const Tin* r2 = r1 + dv.second * a.logits_row_stride;
   float x[EPT];
   if (dv.vec_ok) {
-    uint4 ra[NCH], rb[NCH];
-#pragma unroll
-    for (int j = 0; j < NCH; ++j) {
-      const int id0 = chunk_id(j);
-      ra[j] = make_uint4(0u, 0u, 0u, 0u);
-      rb[j] = make_uint4(0u, 0u, 0u, 0u);
-      if (id0 < V) {
-        ra[j] = __ldcs((const uint4*)(r1 + id0));
-        if (a.cfg_enabled) rb[j] = __ldcs((const uint4*)(r2 + id0));
-      }
-    }
     if (a.cfg_enabled) {
       // three separately rounded scalar ops: ptxas rewrites a packed
       // mul.rn.f32x2 -> add.rn.f32x2 chain, which would change the rounding
