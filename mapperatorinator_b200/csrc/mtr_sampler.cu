@@ -2821,8 +2821,9 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
       bool topk_done = false;
       if (!force_radix) {
         // bound: the chunk maxima in bins <= btau number >= k, so >= k scores lie
-        // within chi of the max.  btau by binary search over the 256 bins: each
-        // probe counts this lane's slots at or below it and sums over the warp.
+        // within chi of the max.  btau from a shared histogram of the 64 nearest
+        // bins; beyond them, a binary search over the 256 bins whose probes count
+        // this lane's slots at or below the probe and sum over the warp.
         uint32_t wbp[NS / 4];  // the slots' bins, four per word (255: empty slot)
 #pragma unroll
         for (int q = 0; q < NS / 4; ++q) {
