@@ -2616,7 +2616,7 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
         float* const Xlo = X + 4 * lane;
         float* const Xhi = X + HALF + 4 * lane;
         u64 kcur = km[0];  // keep bits of slot s in the low byte
-#pragma unroll 2
+#pragma unroll 4
         for (int s = 0; s < NS; ++s) {
           if ((s * 32 + lane) * 8 >= V) break;
           const uint4 ra = *(const uint4*)(Xlo + 128 * s);
