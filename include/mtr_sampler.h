@@ -74,7 +74,8 @@ typedef enum MtrStatus {
 #define MTR_ROW_BAD_UNIFORM (1u << 3) /* uniform outside [0, 1) was clamped      */
 #define MTR_ROW_SLOW_PATH   (1u << 4) /* exact radix fallback was used (info)     */
 #define MTR_ROW_TIE_AT_CUT  (1u << 5) /* the top-p cut split equal scores (info)  */
-#define MTR_ROW_COPY_TIMEOUT (1u << 6) /* a staged row copy never landed; the rest of its CTA's rows were skipped */
+#define MTR_ROW_COPY_TIMEOUT (1u << 6) /* a staged row copy never landed: this row and every later row of
+                                          the same CTA get pad_id and this bit (row-per-warp kernel) */
 
 typedef enum MtrDType { MTR_DTYPE_F32 = 0, MTR_DTYPE_BF16 = 1, MTR_DTYPE_F16 = 2 } MtrDType;
 typedef enum MtrIdType { MTR_IDS_I64 = 0, MTR_IDS_I32 = 1 } MtrIdType;
@@ -111,6 +112,12 @@ typedef enum MtrSelect {
 #define MTR_FLAG_FORCE_RADIX                (1u << 4) /* test hook: always take the exact radix selection path  */
 #define MTR_FLAG_KERNEL_ROW_CTA             (1u << 5) /* use the row-per-CTA kernel (default: chosen by shape)  */
 #define MTR_FLAG_KERNEL_ROW_WARP            (1u << 6) /* use the row-per-warp kernel (V <= 4096, <= 32767 penalty ids) */
+#define MTR_FLAG_KERNEL_STREAM              (1u << 7) /* use the streaming row-group kernel (sampling or processor
+                                                         output with 1 <= top_k <= 64 < V, V % 8 == 0,
+                                                         V <= 65536, 16-byte aligned rows, no column
+                                                         temperatures, grammar given as vocabulary bitmaps) */
+#define MTR_FLAG_TEST_COPY_TIMEOUT          (1u << 8) /* test hook: the row-per-warp kernel's first staged-copy
+                                                         wait gives up at once (exercises MTR_ROW_COPY_TIMEOUT) */
 
 /*
  * All pointer fields are device pointers (host pointers for the CPU oracle
@@ -211,7 +218,7 @@ typedef struct MtrLaunchInfo {
   int32_t max_vocab;      /* MTR_MAX_VOCAB */
   int32_t max_ids_len;    /* MTR_MAX_IDS_LEN */
   int32_t candidate_cap;  /* size of the exact in-bin candidate list */
-  int32_t kernel;         /* 0: row-per-CTA (cluster) kernel, 1: row-per-warp kernel */
+  int32_t kernel;         /* 0: row-per-CTA (cluster) kernel, 1: row-per-warp kernel, 2: streaming row-group kernel */
 } MtrLaunchInfo;
 
 /* ABI identity: MTR_ABI_VERSION and sizeof(MtrSamplerArgs) of the library. */
@@ -228,8 +235,11 @@ int mtr_sampler_validate(const MtrSamplerArgs* args);
 int mtr_sampler_query(int32_t vocab, int32_t num_rows, int32_t with_penalties, MtrLaunchInfo* out);
 
 /* Kernel and geometry mtr_sampler_launch would use for these exact arguments
- * (validates them first).  The row-per-warp kernel is chosen for >= 2 rows per
- * SM of a vocabulary <= 4096 whose selection is argmax or a top-k <= 128. */
+ * (validates them first).  Without a kernel flag the streaming row-group
+ * kernel is chosen whenever it serves the request (see MTR_FLAG_KERNEL_STREAM);
+ * otherwise the row-per-warp kernel for >= 2 rows per SM of a vocabulary
+ * <= 4096 whose selection is argmax or a top-k <= 128, else the row-per-CTA
+ * kernel.  A kernel flag the request does not fit returns MTR_ERR_UNSUPPORTED. */
 int mtr_sampler_query_args(const MtrSamplerArgs* args, MtrLaunchInfo* out);
 
 /*

@@ -59,6 +59,8 @@ FLAG_GRAMMAR_UPDATE_FROM_SAMPLE = 1 << 3
 FLAG_FORCE_RADIX = 1 << 4
 FLAG_KERNEL_ROW_CTA = 1 << 5
 FLAG_KERNEL_ROW_WARP = 1 << 6
+FLAG_KERNEL_STREAM = 1 << 7
+FLAG_TEST_COPY_TIMEOUT = 1 << 8
 
 
 class MtrSamplerArgs(ctypes.Structure):
@@ -141,6 +143,7 @@ class MtrLaunchInfo(ctypes.Structure):
 
 KERNEL_ROW_CTA = 0
 KERNEL_ROW_WARP = 1
+KERNEL_STREAM = 2
 
 
 # Every symbol include/mtr_sampler.h declares: (name, restype, argtypes).

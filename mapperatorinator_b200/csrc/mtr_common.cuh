@@ -1,0 +1,416 @@
+// mtr_common.cuh -- numerics and helpers shared by the kernels of the fused
+// decode-sampling step (mtr_sampler.cu: row-per-CTA and row-per-warp kernels;
+// mtr_stream.cu: streaming row-group kernel).  Every decision-relevant
+// operation lives here once, so all kernels are bit-identical to each other and
+// to the CPU oracle.
+#pragma once
+
+#include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "../../include/mtr_sampler.h"
+
+namespace cg = cooperative_groups;
+
+namespace mtr {
+
+constexpr int NB = 1024;            // distance bins per histogram
+constexpr float BIN_SCALE = 32.0f;  // bins per logit unit (d in [0, 32) before the overflow bin)
+constexpr int CAP = 256;            // candidate list capacity
+constexpr int MINI = 64;            // crossing-bin list capacity
+constexpr int32_t NO_ID = 0x7fffffff;
+constexpr unsigned FULL = 0xffffffffu;
+
+typedef unsigned long long u64;
+
+__device__ __forceinline__ float neg_inf() { return __int_as_float(0xff800000); }
+__device__ __forceinline__ float pos_inf() { return __int_as_float(0x7f800000); }
+
+// ---------------------------------------------------------------------------
+// packed f32x2 arithmetic (sm_100a); each lane is one IEEE round-to-nearest op.
+// Only fma / mul chains are used: they were checked bit-identical to the scalar
+// sequence over every d in the exponential's range and 8M quotients.  ptxas
+// rewrites packed mul -> add chains, so those stay scalar.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ u64 pk2(float a, float b) {
+  u64 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(u64 r, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r)); }
+__device__ __forceinline__ u64 mul2(u64 a, u64 b) {
+  u64 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ u64 fma2(u64 a, u64 b, u64 c) {
+  u64 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// numerics
+// ---------------------------------------------------------------------------
+
+// floor(e^d * 2^31) for d <= 0, by Cody-Waite reduction (ln 2 split into a
+// 16-bit head and a tail) and a degree-6 minimax polynomial on [-ln2/2, ln2/2]
+// with coefficients pre-scaled by 2^31; every step is a single IEEE-rounded
+// operation so the CPU oracle reproduces it bit for bit.
+__device__ __forceinline__ uint32_t expfx(float d) {
+  if (!(d >= -32.0f)) return 0u;
+  const float n = rintf(__fmul_rn(d, 0x1.715476p+0f));
+  float r = __fmaf_rn(-n, 0x1.62e400p-1f, d);
+  r = __fmaf_rn(-n, 0x1.7f7d1cp-20f, r);
+  float p = 0x1.6ab980p+21f;
+  p = __fmaf_rn(p, r, 0x1.126d0cp+24f);
+  p = __fmaf_rn(p, r, 0x1.55589ap+26f);
+  p = __fmaf_rn(p, r, 0x1.55540ap+28f);
+  p = __fmaf_rn(p, r, 0x1.fffffap+29f);
+  p = __fmaf_rn(p, r, 0x1.000000p+31f);
+  p = __fmaf_rn(p, r, 0x1.000000p+31f);
+  const uint32_t m = __float2uint_rz(p);
+  const int sh = -__float2int_rz(n);
+  return sh >= 32 ? 0u : (m >> sh);
+}
+
+// expfx on two values at once (same operations, packed); d0, d1 <= 0
+__device__ __forceinline__ void expfx2(float d0, float d1, uint32_t& q0, uint32_t& q1) {
+  const u64 D = pk2(d0, d1);
+  float t0, t1;
+  up2(mul2(D, pk2(0x1.715476p+0f, 0x1.715476p+0f)), t0, t1);
+  const float n0 = rintf(t0), n1 = rintf(t1);
+  const u64 Nn = pk2(n0, n1);
+  u64 R = fma2(Nn, pk2(-0x1.62e400p-1f, -0x1.62e400p-1f), D);
+  R = fma2(Nn, pk2(-0x1.7f7d1cp-20f, -0x1.7f7d1cp-20f), R);
+  u64 P = pk2(0x1.6ab980p+21f, 0x1.6ab980p+21f);
+  P = fma2(P, R, pk2(0x1.126d0cp+24f, 0x1.126d0cp+24f));
+  P = fma2(P, R, pk2(0x1.55589ap+26f, 0x1.55589ap+26f));
+  P = fma2(P, R, pk2(0x1.55540ap+28f, 0x1.55540ap+28f));
+  P = fma2(P, R, pk2(0x1.fffffap+29f, 0x1.fffffap+29f));
+  P = fma2(P, R, pk2(0x1.000000p+31f, 0x1.000000p+31f));
+  P = fma2(P, R, pk2(0x1.000000p+31f, 0x1.000000p+31f));
+  float p0, p1;
+  up2(P, p0, p1);
+  // |n| <= 46 whenever d >= -32; the clamp only keeps the shift defined
+  const int s0 = -__float2int_rz(fmaxf(n0, -40.0f)), s1 = -__float2int_rz(fmaxf(n1, -40.0f));
+  const uint32_t m0 = __float2uint_rz(p0), m1 = __float2uint_rz(p1);
+  q0 = (d0 >= -32.0f && s0 < 32) ? (m0 >> s0) : 0u;
+  q1 = (d1 >= -32.0f && s1 < 32) ? (m1 >> s1) : 0u;
+}
+
+// x / t correctly rounded, given y = RN(1/t) (Markstein: q0 = x*y, r = x - q0*t
+// exactly, q = q0 + r*y).  Magnitudes outside [2^-60, 2^60) and NaN take the
+// IEEE divide; zeros and infinities pass through (t is positive and finite).
+// out of line: the rare operands keep the IEEE divide away from the hot code
+static __device__ __noinline__ float div_rare(float x, float t) {
+  if (x == 0.0f || fabsf(x) == pos_inf()) return x;
+  return __fdiv_rn(x, t);
+}
+__device__ __forceinline__ float div_by(float x, float t, float y) {
+  const float ax = fabsf(x);
+  if (ax >= 0x1p-60f && ax < 0x1p60f) {
+    const float q0 = __fmul_rn(x, y);
+    const float r = __fmaf_rn(-q0, t, x);
+    return __fmaf_rn(r, y, q0);
+  }
+  return div_rare(x, t);
+}
+
+// the same on a pair; fma(q0, -t, x) is bit-identical to fma(-q0, t, x)
+__device__ __forceinline__ void div_by2(float& x0, float& x1, float t, float y) {
+  const u64 X = pk2(x0, x1), Y = pk2(y, y);
+  const u64 Q0 = mul2(X, Y);
+  const u64 Rr = fma2(Q0, pk2(-t, -t), X);
+  float q0, q1;
+  up2(fma2(Rr, Y, Q0), q0, q1);
+  const float a0 = fabsf(x0), a1 = fabsf(x1);
+  const bool ok0 = a0 >= 0x1p-60f && a0 < 0x1p60f, ok1 = a1 >= 0x1p-60f && a1 < 0x1p60f;
+  const bool pass0 = x0 == 0.0f || a0 == pos_inf(), pass1 = x1 == 0.0f || a1 == pos_inf();
+  if ((!ok0 && !pass0) || (!ok1 && !pass1)) {  // tiny, huge or NaN: rare
+    q0 = ok0 || pass0 ? q0 : __fdiv_rn(x0, t);
+    q1 = ok1 || pass1 ? q1 : __fdiv_rn(x1, t);
+  }
+  x0 = ok0 ? q0 : (pass0 ? x0 : q0);
+  x1 = ok1 ? q1 : (pass1 ? x1 : q1);
+}
+
+// maxima that return NaN when any input is NaN (three-input form: sm_100)
+__device__ __forceinline__ float fmax3n(float a, float b, float c) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float fmax2n(float a, float b) {
+  float d;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+  return d;
+}
+
+static __device__ __noinline__ void div_chunk_rare(float (&v)[8], float t, float y) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = div_by(v[e], t, y);
+}
+
+// x / t for a chunk (y = RN(1/t)): Markstein on pairs when every value that is
+// not -inf lies in [2^-60, 2^60) (-inf passes through), the IEEE divide per
+// element otherwise.
+__device__ __forceinline__ void div_chunk(float (&v)[8], float t, float y) {
+  float w[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) w[e] = v[e] == neg_inf() ? 1.0f : fabsf(v[e]);
+  const float amax = fmax3n(fmax3n(w[0], w[1], w[2]), fmax3n(w[3], w[4], w[5]), fmax2n(w[6], w[7]));
+  const float amin = fminf(fminf(fminf(w[0], w[1]), fminf(w[2], w[3])), fminf(fminf(w[4], w[5]), fminf(w[6], w[7])));
+  if (amax < 0x1p60f && amin >= 0x1p-60f) {
+    const u64 Y = pk2(y, y), NT = pk2(-t, -t);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      const u64 Xv = pk2(v[e], v[e + 1]);
+      const u64 Q0 = mul2(Xv, Y);
+      float q0, q1;
+      up2(fma2(fma2(Q0, NT, Xv), Y, Q0), q0, q1);
+      v[e] = v[e] == neg_inf() ? v[e] : q0;
+      v[e + 1] = v[e + 1] == neg_inf() ? v[e + 1] : q1;
+    }
+  } else {
+    div_chunk_rare(v, t, y);
+  }
+}
+
+// order-preserving key of a non-NaN float (-0 and +0 share a key)
+__device__ __forceinline__ uint32_t fkey(float x) {
+  uint32_t u = __float_as_uint(x);
+  if (x == 0.0f) u = 0u;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// distance bin of a finite x below the row maximum mx (non-increasing in x).
+// bin(x) <= b  <=>  (mx - x) < (b + 1) / BIN_SCALE for b < NB - 1 (the scaling
+// by a power of two is exact).
+__device__ __forceinline__ int dbin(float mx, float x) {
+  float s = __fmul_rn(__fsub_rn(mx, x), BIN_SCALE);
+  s = fminf(s, (float)(NB - 1));
+  return __float2int_rz(s);
+}
+
+__device__ __forceinline__ bool finite_val(float x) { return fabsf(x) < pos_inf(); }
+
+// Hint: pull [p, p + bytes) into L2 with one bulk prefetch (16-byte granules
+// fully inside the range; nothing is read into the SM).
+__device__ __forceinline__ void l2_prefetch(const void* p, size_t bytes) {
+  const uintptr_t b0 = ((uintptr_t)p + 15u) & ~(uintptr_t)15u;
+  const uintptr_t b1 = ((uintptr_t)p + bytes) & ~(uintptr_t)15u;
+  if (b1 > b0 && b1 - b0 < (1u << 20))
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(b0), "r"((uint32_t)(b1 - b0)) : "memory");
+}
+
+// canonical order: higher score first, then lower token id
+__device__ __forceinline__ bool canon_before(float xj, int32_t ij, float xi, int32_t ii) {
+  return xj > xi || (xj == xi && ij < ii);
+}
+
+// ---------------------------------------------------------------------------
+// element loads
+// ---------------------------------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static constexpr int VEC = 4;
+  __device__ static float get(const uint4& w, int e) {
+    const uint32_t v = e == 0 ? w.x : e == 1 ? w.y : e == 2 ? w.z : w.w;
+    return __uint_as_float(v);
+  }
+  __device__ static float one(const void* p, int64_t i) { return __ldcs((const float*)p + i); }
+  // the 16-byte group starting at element i from scalar loads (ids >= V read as 0)
+  __device__ static uint4 gather(const void* p, int i, int V) {
+    const float* f = (const float*)p;
+    uint4 r;
+    r.x = i < V ? __float_as_uint(__ldcs(f + i)) : 0u;
+    r.y = i + 1 < V ? __float_as_uint(__ldcs(f + i + 1)) : 0u;
+    r.z = i + 2 < V ? __float_as_uint(__ldcs(f + i + 2)) : 0u;
+    r.w = i + 3 < V ? __float_as_uint(__ldcs(f + i + 3)) : 0u;
+    return r;
+  }
+};
+// 16-bit types: the 16-byte group of 8 elements from scalar loads (ids >= V read as 0)
+__device__ __forceinline__ uint4 gather_u16(const void* p, int i, int V) {
+  const unsigned short* h = (const unsigned short*)p;
+  uint32_t w[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t lo = i + 2 * k < V ? (uint32_t)__ldcs(h + i + 2 * k) : 0u;
+    const uint32_t hi = i + 2 * k + 1 < V ? (uint32_t)__ldcs(h + i + 2 * k + 1) : 0u;
+    w[k] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+template <> struct Elem<__nv_bfloat16> {
+  static constexpr int VEC = 8;
+  __device__ static float get(const uint4& w, int e) {
+    const uint32_t v = (e >> 1) == 0 ? w.x : (e >> 1) == 1 ? w.y : (e >> 1) == 2 ? w.z : w.w;
+    return __uint_as_float((e & 1) ? (v & 0xffff0000u) : (v << 16));
+  }
+  __device__ static float one(const void* p, int64_t i) {
+    const unsigned short h = __ldcs((const unsigned short*)p + i);
+    return __uint_as_float((uint32_t)h << 16);
+  }
+  __device__ static uint4 gather(const void* p, int i, int V) { return gather_u16(p, i, V); }
+};
+template <> struct Elem<__half> {
+  static constexpr int VEC = 8;
+  __device__ static float get(const uint4& w, int e) {
+    const uint32_t v = (e >> 1) == 0 ? w.x : (e >> 1) == 1 ? w.y : (e >> 1) == 2 ? w.z : w.w;
+    const unsigned short h = (e & 1) ? (unsigned short)(v >> 16) : (unsigned short)(v & 0xffffu);
+    return __half2float(__ushort_as_half(h));
+  }
+  __device__ static float one(const void* p, int64_t i) {
+    const unsigned short h = __ldcs((const unsigned short*)p + i);
+    return __half2float(__ushort_as_half(h));
+  }
+  __device__ static uint4 gather(const void* p, int i, int V) { return gather_u16(p, i, V); }
+};
+
+__device__ __forceinline__ int64_t load_id(const MtrSamplerArgs& a, int64_t row, int64_t pos) {
+  const int64_t off = row * a.ids_row_stride + pos;
+  if (a.ids_dtype == MTR_IDS_I32) return (int64_t)__ldg((const int32_t*)a.input_ids + off);
+  return (int64_t)__ldg((const long long*)a.input_ids + off);
+}
+
+__device__ __forceinline__ bool is_sos(const MtrSamplerArgs& a, int64_t t) {
+  bool s = false;
+#pragma unroll 1
+  for (int i = 0; i < a.n_sos; ++i) s |= (t == (int64_t)a.sos_ids[i]);
+  return s;
+}
+
+__device__ __forceinline__ int32_t mono_update(const MtrSamplerArgs& a, int32_t s, int64_t t) {
+  if (t >= a.ts_start && t < a.ts_end) return (int32_t)(t - a.ts_start);
+  if (is_sos(a, t)) return -1;
+  return s;
+}
+
+__device__ __forceinline__ bool is_eos(const MtrSamplerArgs& a, int64_t t) {
+  bool e = false;
+#pragma unroll 1
+  for (int i = 0; i < a.n_eos; ++i) e |= (t == (int64_t)a.eos_ids[i]);
+#pragma unroll 1
+  for (int i = 0; i < a.n_eos_ranges; ++i) e |= (t >= a.eos_range_start[i] && t < a.eos_range_end[i]);
+  return e;
+}
+
+// bits [lo, hi) of an 8-bit chunk mask (empty when hi <= lo)
+__device__ __forceinline__ uint32_t range_bits(int lo, int hi) {
+  lo = max(lo, 0);
+  hi = min(hi, 8);
+  return hi > lo ? (((1u << hi) - 1u) & ~((1u << lo) - 1u)) : 0u;
+}
+
+// ---------------------------------------------------------------------------
+// cluster helper: CS == 1 degenerates to the CTA
+// ---------------------------------------------------------------------------
+// ---------------------------------------------------------------------------
+// warp / block helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ u64 warp_sum_u64(u64 v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+  return v;
+}
+__device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+  return v;
+}
+__device__ __forceinline__ u64 warp_incl_scan_u64(u64 v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const u64 t = __shfl_up_sync(FULL, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+__device__ __forceinline__ uint32_t warp_incl_scan_u32(uint32_t v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(FULL, v, o);
+    if (lane >= o) v += t;
+  }
+  return v;
+}
+
+
+// Host-derived constants of one launch.
+struct Derived {
+  int64_t second;    // rows between a first-half row and its partner
+  int32_t pen_on;
+  int32_t vec_ok;    // 16-byte loads of logits allowed
+  int32_t cls_vec;   // vector loads of grammar_class_of allowed
+  int32_t out_vec;   // float4 stores of out_scores allowed
+  int32_t lp_vec;    // float4 stores of out_logprobs allowed
+  int32_t topk_on;
+  int32_t topp_on;
+  int32_t ids_len;
+  int32_t id_shift;  // id >> id_shift < NB for every id < V
+  int32_t gwords;    // 32-bit words per grammar vocabulary bitmap
+  float temp_rcp;
+  float cond_rcp[MTR_MAX_COND_TEMPS];
+  float col_rcp[MTR_MAX_COL_TEMP_RANGES];
+  // -1, -0 and 1 as launch parameters: FMAs with them stay FMAs (a compile-time
+  // constant would let the compiler turn them into a mul + add pair and fuse it)
+  float neg_one, neg_zero, one;
+  float rep_rcp;  // RN(1 / repetition_penalty) when it lies in [2^-30, 2^30] (Markstein divide), else 0
+};
+
+// Warp bitonic sort of 32*E distinct (or zero) u64 keys, descending; lane l
+// holds positions l*E .. l*E+E-1.
+
+// Bitonic sort of 64 u64 keys held two per lane (positions 2*lane, 2*lane+1), descending.
+__device__ __forceinline__ void sort64_desc(u64& a0, u64& a1, int lane) {
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j >= 2; j >>= 1) {
+      const u64 p0 = __shfl_xor_sync(FULL, a0, j >> 1), p1 = __shfl_xor_sync(FULL, a1, j >> 1);
+      const int g = 2 * lane;  // both positions share the bits k and j
+      const bool keep_larger = ((g & k) == 0) == ((g & j) == 0);
+      // keys are distinct except the empty (zero) entries, where taking either is the same
+      if ((p0 > a0) == keep_larger) a0 = p0;
+      if ((p1 > a1) == keep_larger) a1 = p1;
+    }
+    const bool desc = ((2 * lane) & k) == 0;
+    const bool sw = (a0 < a1) == desc;
+    const u64 t0 = sw ? a1 : a0, t1 = sw ? a0 : a1;
+    a0 = t0;
+    a1 = t1;
+  }
+}
+// repetition (x < 0 ? x * rp : x / rp), then frequency and presence, each step
+// skipped when it is the identity (rp = 1, fp = 0, pp = 0); y = RN(1 / rp) or 0
+__device__ __forceinline__ float pen_value(float x, float c, float rp, float fp, float pp, float y) {
+  if (rp != 1.0f) x = x < 0.0f ? __fmul_rn(x, rp) : (y != 0.0f ? div_by(x, rp, y) : div_rare(x, rp));
+  if (fp != 0.0f) x = __fsub_rn(x, __fmul_rn(fp, c));
+  if (pp != 0.0f) x = __fsub_rn(x, pp);
+  return x;
+}
+
+// Host side shared by the translation units of the library.
+// Occupancy of a kernel at a launch shape, per device (computed once).
+cudaError_t cached_occupancy(const void* kern, int threads, int dyn, int* occ);
+
+// The streaming row-group kernel (mtr_stream.cu): whether it serves a request,
+// its launch, and its launch shape for mtr_sampler_query_args.
+bool sk_supported(const MtrSamplerArgs& a, const Derived& d);
+cudaError_t stream_launch(const MtrSamplerArgs& a, const Derived& d, int sms, cudaStream_t s);
+void stream_query(const MtrSamplerArgs& a, const Derived& d, int sms, MtrLaunchInfo* out);
+
+}  // namespace mtr

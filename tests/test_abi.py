@@ -144,13 +144,20 @@ def test_query_geometry(lib, vocab, rows, cs):
 
 @pytest.mark.parametrize("rows,vocab,top_k,select,flags,kernel", [
     (4096, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_WARP),      # many rows, short top-k list
-    (4096, 4096, 0, N.SELECT_ARGMAX, 0, N.KERNEL_ROW_WARP),
     (64, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),         # few rows: latency geometry
+    (256, 65536, 50, N.SELECT_SAMPLE, 0, N.KERNEL_STREAM),        # large vocabulary: 16 warps per row
+    (256, 16384, 50, N.SELECT_NONE, 0, N.KERNEL_STREAM),          # processor output with top-k
+    (4096, 8192, 50, N.SELECT_SAMPLE, 0, N.KERNEL_STREAM),
+    (4096, 4096, 0, N.SELECT_ARGMAX, 0, N.KERNEL_ROW_WARP),
+    (4096, 4096, 100, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_WARP),     # top-k past the stream kernel's 64
+    (4096, 16384, 100, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),     # large vocabulary, long top-k list
     (4096, 4096, 0, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),        # top-p over the whole row
     (4096, 4096, 500, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),      # long top-k list
-    (4096, 8192, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),       # vocabulary above 4096
+    (4096, 131072, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),     # vocabulary above 65536
     (4096, 4096, 50, N.SELECT_SAMPLE, N.FLAG_KERNEL_ROW_CTA, N.KERNEL_ROW_CTA),
+    (4096, 4096, 50, N.SELECT_SAMPLE, N.FLAG_KERNEL_ROW_WARP, N.KERNEL_ROW_WARP),
     (8, 4096, 0, N.SELECT_SAMPLE, N.FLAG_KERNEL_ROW_WARP, N.KERNEL_ROW_WARP),
+    (8, 4096, 5, N.SELECT_SAMPLE, N.FLAG_KERNEL_STREAM, N.KERNEL_STREAM),
 ])
 def test_query_args_kernel_choice(lib, rows, vocab, top_k, select, flags, kernel):
     a = _valid_args()
@@ -165,6 +172,18 @@ def test_query_args_kernel_choice(lib, rows, vocab, top_k, select, flags, kernel
         assert info.dyn_smem_bytes <= 48 * 1024
         if vocab == 4096:  # ten one-warp CTAs per SM: 228 KB, per CTA 1 KB reserved + 16 B static, 128 B units
             assert (info.dyn_smem_bytes + 16 + 127) // 128 * 128 * 10 + 10 * 1024 <= 228 * 1024
+    elif kernel == N.KERNEL_STREAM:
+        # row groups of G warps (G * 32 threads * 16 chunks * 8 ids >= V), persistent grid
+        assert info.threads in (128, 256, 512) and info.cluster_size == 1
+        assert info.candidate_cap == 256
+        groups_per_cta = max(1, 128 // info.threads)
+        g_threads = info.threads // groups_per_cta
+        assert g_threads * info.elems_per_thread >= vocab
+        assert info.grid * groups_per_cta <= rows + groups_per_cta
+        if vocab == 65536:
+            # sixteen warps per row, two CTAs per SM within 228 KB
+            assert info.threads == 512
+            assert 2 * (info.dyn_smem_bytes + 1024) <= 228 * 1024
     else:
         assert info.grid == rows * info.cluster_size
 
@@ -173,11 +192,25 @@ def test_kernel_flags_validated(lib):
     a = _valid_args()
     a.flags = N.FLAG_KERNEL_ROW_CTA | N.FLAG_KERNEL_ROW_WARP
     assert N.validate(a) == N.ERR_BAD_PARAM
+    a.flags = N.FLAG_KERNEL_ROW_WARP | N.FLAG_KERNEL_STREAM
+    assert N.validate(a) == N.ERR_BAD_PARAM
     a.flags = N.FLAG_KERNEL_ROW_WARP
     a.vocab = a.logits_row_stride = 4097
     assert N.validate(a) == N.ERR_UNSUPPORTED
     a.vocab = a.logits_row_stride = 4096
     assert N.validate(a) == N.OK
+    # the streaming kernel: top-k in [1, 64], sampling or processor output, V % 8 == 0
+    a.flags = N.FLAG_KERNEL_STREAM
+    a.top_k = 50
+    assert N.validate(a) == N.OK
+    for field, value in (("top_k", 0), ("top_k", 65), ("select_mode", N.SELECT_ARGMAX), ("vocab", 4100),
+                         ("temp_mode", N.TEMP_COLUMN_RANGES)):
+        b = _valid_args()
+        b.flags, b.top_k = N.FLAG_KERNEL_STREAM, 50
+        setattr(b, field, value)
+        if field == "vocab":
+            b.logits_row_stride = value
+        assert N.validate(b) == N.ERR_UNSUPPORTED, field
 
 
 def test_status_strings(lib):

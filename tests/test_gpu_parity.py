@@ -6,30 +6,38 @@ import pytest
 
 from mapperatorinator_b200 import _native as N
 from mapperatorinator_b200 import workloads as W
-from mapperatorinator_b200.stepargs import DeviceStep
+from mapperatorinator_b200.stepargs import DeviceStep, fill_args, host_arrays
 from oracle import oracle
 from tests import _golden as G
 
 pytestmark = pytest.mark.gpu
 
-_KERNEL_FLAGS = {"cta": N.FLAG_KERNEL_ROW_CTA, "warp": N.FLAG_KERNEL_ROW_WARP}
+_KERNEL_FLAGS = {"cta": N.FLAG_KERNEL_ROW_CTA, "warp": N.FLAG_KERNEL_ROW_WARP, "stream": N.FLAG_KERNEL_STREAM}
+_ALL_KERNEL_FLAGS = N.FLAG_KERNEL_ROW_CTA | N.FLAG_KERNEL_ROW_WARP | N.FLAG_KERNEL_STREAM
 _kernel = {"name": "cta"}
 
 
-@pytest.fixture(autouse=True, params=["cta", "warp"])
+@pytest.fixture(autouse=True, params=["cta", "warp", "stream"])
 def kernel(request):
-    """Every parity case runs on both kernels (the row-per-warp kernel takes
-    vocabularies up to 4096 only)."""
+    """Every parity case runs on every kernel that serves it (the row-per-warp
+    kernel takes vocabularies up to 4096; the streaming kernel a top-k in
+    [1, 64] with sampling or processor output)."""
     _kernel["name"] = request.param
     yield request.param
     _kernel["name"] = "cta"
 
 
 def forced(s):
-    """`s` with the current kernel forced; skips vocabularies the kernel does not take."""
+    """`s` with the current kernel forced; skips requests the kernel does not serve."""
     if _kernel["name"] == "warp" and s.vocab > 4096:
         pytest.skip("row-per-warp kernel: vocab <= 4096")
-    return s.with_(flags=(s.flags & ~(N.FLAG_KERNEL_ROW_CTA | N.FLAG_KERNEL_ROW_WARP)) | _KERNEL_FLAGS[_kernel["name"]])
+    s = s.with_(flags=(s.flags & ~_ALL_KERNEL_FLAGS) | _KERNEL_FLAGS[_kernel["name"]])
+    if _kernel["name"] == "stream":
+        arrays = host_arrays(s)
+        args = fill_args(N.new_args(), s, lambda k: arrays[k].ctypes.data if k in arrays else 0)
+        if N.validate(args) == N.ERR_UNSUPPORTED:
+            pytest.skip("streaming kernel does not serve this request")
+    return s
 
 
 def run_both(s, device):
