@@ -25,7 +25,6 @@ import argparse
 import json
 import math
 import os
-import re
 import sys
 import threading
 import time
@@ -180,15 +179,6 @@ def measured_peak():
     return 6650.0, "fallback"
 
 
-def profiled_traffic():
-    """dram bytes per launch from the committed ncu summary, if one exists."""
-    p = ROOT / "profiles" / "sampler_sharded_decode_ncu.md"
-    if not p.exists():
-        return None
-    m = re.search(r"dram_bytes_per_full_launch:\s*([0-9.eE+]+)", p.read_text())
-    return float(m.group(1)) if m else None
-
-
 def make_tables(gen, device):
     class_of = torch.randint(0, N_CLASSES, (VOCAB,), generator=gen, device=device).to(torch.uint8)
     table = torch.rand((N_CLASSES, N_CLASSES), generator=gen, device=device) < 0.5
@@ -284,9 +274,6 @@ def run_ours(args, dist: Dist):
     bytes_launch = algorithmic_bytes(pairs)
     peak, peak_kind = measured_peak()
     achieved = bytes_launch / per_launch_s / 1e9
-    traffic = profiled_traffic()
-    if traffic is not None:
-        traffic = traffic / dist.world  # the summary is for the 1-GPU launch; rows scale linearly
 
     # ---- end to end through FusedSampler with host buffers
     e2e_steps = max(1, min(args.e2e_steps, args.steps))
@@ -329,7 +316,8 @@ def run_ours(args, dist: Dist):
                        "l2": f"logits rotate over {nbuf} buffers ({nbuf * buf_bytes / 2**20:.0f} MiB per GPU, "
                              f"> 3x L2)", "graph": f"{args.steps} launches captured in one CUDA graph"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "traffic_note": "DRAM bytes per launch come from an ncu capture (profiles/), not from this run",
                          "algorithmic_bytes_per_launch": bytes_launch, "kernel": kernel_name,
                          "grid": info.grid, "threads": info.threads,
                          "avg_launch_us": per_launch_s * 1e6},
@@ -383,41 +371,66 @@ def run_b64(args, device, stream, dist, profile=0):
 
 
 # ---------------------------------------------------------------- CPU side
-def _cpu_chain_inputs(pairs, seed=5):
-    from oracle.torch_chain import ChainParams
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def _cpu_chain(pairs, seed=5):
+    """The sharded_decode chain on the host, returned as (step function, kind).
+
+    kind "reference": the reference's own processors, path-loaded from the
+    unmodified copy in baseline/_ref (baseline/install_reference.sh) --
+    build_logits_processor_list (HF ClassifierFreeGuidance + the reference's
+    MonotonicTimeShift) and HF's RepetitionPenalty / TopK / TopP, then softmax +
+    torch.multinomial as the reference's decode loop does.  The event-grammar
+    mask and the frequency / presence penalties have no reference
+    implementation and come from oracle/torch_chain.py.  kind "port": the whole
+    chain from oracle/torch_chain.py (when baseline/_ref is absent)."""
+    from oracle import torch_chain as TC
 
     g = torch.Generator().manual_seed(seed)
     class_of = torch.randint(0, N_CLASSES, (VOCAB,), generator=g)
     table = torch.rand((N_CLASSES, N_CLASSES), generator=g) < 0.5
     table[:, 0] = True
-    prm = ChainParams(cfg_scale=1.5, ts_range=(0, TS_END), sos_ids=(SOS_ID,), grammar_class_of=class_of,
-                      grammar_table=table, repetition_penalty=1.1, frequency_penalty=0.2, presence_penalty=0.1,
-                      top_k=50, top_p=0.95)
     logits = (torch.randn((2 * pairs, VOCAB), generator=g) * 2.0).to(torch.bfloat16)
     ids = torch.randint(0, VOCAB, (pairs, HISTORY), generator=g)
-    # a time shift late in each history so the monotonic mask is active
-    ids[:, -2] = torch.randint(0, TS_END, (pairs,), generator=g)
+    ids[:, -2] = torch.randint(0, TS_END, (pairs,), generator=g)  # a late time shift: the monotonic mask is active
     prev = torch.randint(0, VOCAB, (pairs,), generator=g)
-    return prm, logits, ids, prev, g
+    try:
+        from oracle.reference_loader import load_reference, make_tokenizer
+        from transformers import RepetitionPenaltyLogitsProcessor, TopKLogitsWarper, TopPLogitsWarper
 
+        ev, lp, _sl, _ = load_reference(REF_DIR)
+    except (FileNotFoundError, ImportError):
+        prm = TC.ChainParams(cfg_scale=1.5, ts_range=(0, TS_END), sos_ids=(SOS_ID,), grammar_class_of=class_of,
+                             grammar_table=table, repetition_penalty=1.1, frequency_penalty=0.2,
+                             presence_penalty=0.1, top_k=50, top_p=0.95)
+        return (lambda: TC.sample_step(logits, ids, prm, prev_tokens=prev, generator=g)), "port"
+    tok = make_tokenizer(ev, ts=(0, TS_END), sos=SOS_ID)
+    procs = lp.build_logits_processor_list(tok, cfg_scale=1.5, types_first=False, temperature=1.0)
+    rep, topk, topp = RepetitionPenaltyLogitsProcessor(1.1), TopKLogitsWarper(50), TopPLogitsWarper(0.95)
 
-def _cpu_step(prm, logits, ids, prev, g):
-    from oracle.torch_chain import sample_step
+    def step():
+        scores = procs(ids, logits.to(torch.float32))
+        scores = TC.grammar_mask(scores, prev, class_of, table)
+        scores = rep(ids, scores)
+        scores = TC.frequency_presence(scores, ids, 0.2, 0.1)
+        scores = topp(ids, topk(ids, scores))
+        return torch.multinomial(torch.nn.functional.softmax(scores, dim=-1), 1, generator=g).squeeze(1)
 
-    return sample_step(logits, ids, prm, prev_tokens=prev, generator=g)
+    return step, "reference"
 
 
 def cpu_baseline(seconds: float, pairs: int = 64):
-    """PyTorch restatement of the reference chain on the host cores."""
+    """The reference chain on the host cores (bounded sample of the workload)."""
     torch.set_num_threads(os.cpu_count() or 1)
-    prm, logits, ids, prev, g = _cpu_chain_inputs(pairs)
-    _cpu_step(prm, logits, ids, prev, g)
+    step, kind = _cpu_chain(pairs)
+    step()
     n, t0 = 0, time.perf_counter()
     while time.perf_counter() - t0 < seconds and n < 500:
-        _cpu_step(prm, logits, ids, prev, g)
+        step()
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": pairs / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": pairs / dt, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": kind,
             "sample": f"{pairs} CFG pairs of the sharded_decode chain per step, {n} steps, "
                       f"torch {torch.__version__} CPU, {dt * 1e3:.1f} ms/step"}
 
@@ -426,29 +439,31 @@ def run_reference(args, dist: Dist):
     if dist.rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    prm, logits, ids, prev, g = _cpu_chain_inputs(64)
+    step, kind = _cpu_chain(64)
     t = time.perf_counter()
-    _cpu_step(prm, logits, ids, prev, g)
+    step()
     t64 = time.perf_counter() - t
     budget = 120.0
     pairs = int(max(1, min(64, math.floor(64 * budget / max(1e-9, args.steps * t64)))))
-    prm, logits, ids, prev, g = _cpu_chain_inputs(pairs)
+    step, kind = _cpu_chain(pairs)
     for _ in range(args.warmup):
-        _cpu_step(prm, logits, ids, prev, g)
+        step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        _cpu_step(prm, logits, ids, prev, g)
+        step()
     dt = time.perf_counter() - t0
     value = pairs * args.steps / dt
     cores = torch.get_num_threads()
-    sample = (f"{pairs} CFG pairs of the sharded_decode chain per step (PyTorch CPU restatement of the reference "
-              f"processors + softmax + multinomial), {args.steps} steps")
+    what = ("the reference's own processors (build_logits_processor_list, HF repetition / top-k / top-p) + "
+            "grammar and frequency / presence from oracle/torch_chain.py" if kind == "reference" else
+            "PyTorch CPU restatement of the reference chain (oracle/torch_chain.py)")
+    sample = f"{pairs} CFG pairs of the sharded_decode chain per step ({what}), softmax + multinomial, {args.steps} steps"
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": dist.world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
             "data": "synthetic: seeded N(0, 2^2) bf16 logits, uniform 512-id histories",
             "config": {"workload": WORKLOAD, "global_batch": PAIRS, "sample_pairs_per_step": pairs},
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 

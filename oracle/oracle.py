@@ -14,8 +14,8 @@ from pathlib import Path
 import numpy as np
 
 from mapperatorinator_b200 import _native as N
-from mapperatorinator_b200.stepargs import STATE_KEYS, fill_args, host_arrays
-from mapperatorinator_b200.workloads import StepInputs
+from tests.harness.stepargs import STATE_KEYS, fill_args, host_arrays
+from tests.harness.workloads import StepInputs
 
 ORACLE_DIR = Path(__file__).resolve().parent
 LIB = ORACLE_DIR / "_build" / "libmtr_oracle.so"

@@ -9,7 +9,7 @@ from pathlib import Path
 import numpy as np
 
 from mapperatorinator_b200 import _native as N
-from mapperatorinator_b200.workloads import StepInputs, bf16_bits
+from tests.harness.workloads import StepInputs, bf16_bits
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "reference_chain.npz"
 CHAIN_CASES = ("chain_cfg_mono_temp", "chain_condtemp", "chain_condtemp_b1", "chain_bias_cfg2", "chain_c0_shape",
@@ -86,14 +86,14 @@ def explain_keep_mismatch(scores: np.ndarray, ref_keep: np.ndarray, got_keep: np
     """True when a keep-set difference in one row is a tie at the cut or a
     cumulative mass within `margin` of top_p (float64 reference mass).
 
-    With ``status`` None the tie is read from the data: every differing token
-    has the score of the smallest kept score."""
+    A tie at the cut: every differing token has the score of the smallest
+    kept score (the group the two sides split at different ids).  When the
+    kernel's ``status`` is given it must also carry MTR_ROW_TIE_AT_CUT for the
+    tie to excuse the difference; the flag alone excuses nothing."""
     diff_ids = np.nonzero(ref_keep != got_keep)[0]
-    if status is None:
-        cut = min(scores[ref_keep].min(), scores[got_keep].min())
-        if (scores[diff_ids] == cut).all():
-            return True
-    elif status & N.ROW_TIE_AT_CUT:
+    cut = min(scores[ref_keep].min(), scores[got_keep].min())
+    tie = bool((scores[diff_ids] == cut).all())
+    if tie and (status is None or status & N.ROW_TIE_AT_CUT):
         return True
     fin = np.isfinite(scores)
     x = scores[fin].astype(np.float64)

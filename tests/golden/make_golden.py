@@ -1,10 +1,10 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Run in a checkout that has the Mapperatorinator sources (default
-/root/reference, override with MTR_REFERENCE_DIR) and the transformers
-package installed:
+Run where the Mapperatorinator sources are available -- MTR_REFERENCE_DIR,
+or the copy that baseline/install_reference.sh places in baseline/_ref --
+with the transformers package installed:
 
-    python tests/golden/make_golden.py
+    MTR_REFERENCE_DIR=<reference checkout> python tests/golden/make_golden.py
 
 It imports the reference's own processor modules by path -- the package
 ``__init__`` files pull in dependencies that are not needed here, so the
@@ -21,49 +21,34 @@ reads the reference checkout.
 
 from __future__ import annotations
 
-import ast
 import json
 import os
 import sys
-import types
 from pathlib import Path
 
 import numpy as np
 import torch
 
-REF = Path(os.environ.get("MTR_REFERENCE_DIR", "/root/reference"))
+ROOT = Path(__file__).resolve().parents[2]
 OUT = Path(__file__).resolve().parent / "reference_chain.npz"
+sys.path.insert(0, str(ROOT))
+from oracle.reference_loader import load_reference as _load_reference  # noqa: E402
+from oracle.reference_loader import make_tokenizer  # noqa: E402
 
 
-def _stub_pkg(name: str, path: Path) -> None:
-    mod = types.ModuleType(name)
-    mod.__path__ = [str(path)]
-    sys.modules[name] = mod
+def reference_dir() -> Path:
+    """MTR_REFERENCE_DIR, else the copy placed by baseline/install_reference.sh."""
+    env = os.environ.get("MTR_REFERENCE_DIR")
+    ref = Path(env) if env else ROOT / "baseline" / "_ref"
+    if not (ref / "osuT5").exists():
+        raise SystemExit(f"reference sources not found at {ref}: set MTR_REFERENCE_DIR or run "
+                         "baseline/install_reference.sh")
+    return ref
 
 
 def load_reference():
-    _stub_pkg("osuT5", REF / "osuT5")
-    _stub_pkg("osuT5.osuT5", REF / "osuT5" / "osuT5")
-    _stub_pkg("osuT5.osuT5.inference", REF / "osuT5" / "osuT5" / "inference")
-    _stub_pkg("osuT5.osuT5.inference.optimized", REF / "osuT5" / "osuT5" / "inference" / "optimized")
-    _stub_pkg("osuT5.osuT5.inference.optimized.single",
-              REF / "osuT5" / "osuT5" / "inference" / "optimized" / "single")
-    _stub_pkg("osuT5.osuT5.dataset", REF / "osuT5" / "osuT5" / "dataset")
-    du = types.ModuleType("osuT5.osuT5.dataset.data_utils")
-    du.TIMED_EVENTS = []
-    sys.modules[du.__name__] = du
-    tk = types.ModuleType("osuT5.osuT5.tokenizer")
-    tk.MILISECONDS_PER_STEP = 10
-    tk.Tokenizer = object
-    sys.modules[tk.__name__] = tk
-    import osuT5.osuT5.event as ev
-    import osuT5.osuT5.inference.logit_processors as lp
-    import osuT5.osuT5.inference.optimized.single.logits as sl
+    return _load_reference(reference_dir())
 
-    src = (REF / "osuT5" / "osuT5" / "inference" / "compiled_decode.py").read_text()
-    tree = ast.parse(src)
-    fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "_sample")
-    return ev, lp, sl, ast.Module(body=[fn], type_ignores=[])
 
 
 class _TorchObserver:
@@ -86,23 +71,6 @@ def run_sample(fn_module, logits, do_sample, top_p, top_k, temperature):
     exec(compile(fn_module, "compiled_decode._sample", "exec"), ns)
     out = ns["_sample"](logits.clone(), do_sample, top_p, top_k, temperature)
     return out, obs.probs
-
-
-def make_tokenizer(ev, *, ts=(16, 116), sos=1, context_sos=None, extra=None):
-    class Tok:
-        pass
-
-    t = Tok()
-    t.sos_id = sos
-    t.eos_id = 2
-    t.context_sos = dict(context_sos or {})
-    t.context_eos = {}
-    t.event_start = {ev.EventType.TIME_SHIFT: ts[0]}
-    t.event_end = {ev.EventType.TIME_SHIFT: ts[1]}
-    for name, (a, b) in (extra or {}).items():
-        t.event_start[ev.EventType[name]] = a
-        t.event_end[ev.EventType[name]] = b
-    return t
 
 
 def hf_warpers(scores, top_k, top_p):
@@ -236,6 +204,77 @@ def main() -> None:
     put("hf_repetition", logits=x.numpy(), input_ids=ids.numpy(), processed=rep.numpy(),
         final_hf=hf_warpers(rep.clone(), 50, 0.95).numpy())
     meta["hf_repetition"] = {"penalty": 1.1, "top_k": 50, "top_p": 0.95}
+
+    # ---- the reference's decode loop on scripted one-hot logits: pad-on-finished and
+    # wait-for-all-rows (the scenario of tests/test_optimized_single_decode_loop_migration.py:297-324,
+    # greedy, EOS 2, pad 0, V = 8), plus seeded random schedules ----
+    import importlib
+    from types import SimpleNamespace
+
+    from transformers import StoppingCriteriaList
+
+    dl = importlib.import_module("osuT5.osuT5.inference.optimized.single.decode_loop")
+
+    class Scripted:
+        """A decoder whose step t puts logit +1000 on schedule[t][row], -1000 elsewhere."""
+
+        def __init__(self, schedule, vocab):
+            self.schedule = schedule
+            self.vocab = vocab
+            self.t = 0
+            self.config = SimpleNamespace(is_encoder_decoder=False, _attn_implementation="sdpa")
+
+        def _get_initial_cache_position(self, cur_len, device, model_kwargs):
+            return model_kwargs
+
+        def _valid_auto_compile_criteria(self, model_kwargs, generation_config):
+            return False
+
+        def _has_unfinished_sequences(self, finished, synced_gpus, device):
+            return not bool(finished)
+
+        def prepare_inputs_for_generation(self, input_ids, **model_kwargs):
+            return {"input_ids": input_ids[:, -1:], "decoder_attention_mask": model_kwargs["decoder_attention_mask"]}
+
+        def __call__(self, **kwargs):
+            tokens = torch.tensor(self.schedule[self.t])
+            self.t += 1
+            logits = torch.full((len(tokens), 1, self.vocab), -1000.0)
+            logits[torch.arange(len(tokens)), 0, tokens] = 1000.0
+            return SimpleNamespace(logits=logits)
+
+        def _update_model_kwargs_for_generation(self, outputs, model_kwargs, is_encoder_decoder):
+            mask = model_kwargs["decoder_attention_mask"]
+            model_kwargs["decoder_attention_mask"] = torch.cat((mask, torch.ones((mask.shape[0], 1), dtype=mask.dtype)), 1)
+            return model_kwargs
+
+    class RowEos:
+        eos_token_id = 2
+
+        def __call__(self, input_ids, scores):
+            return input_ids[:, -1].eq(self.eos_token_id)
+
+    def decode_case(name, schedule, prompt):
+        steps = len(schedule)
+        cfg = SimpleNamespace(return_dict_in_generate=False, output_attentions=False, output_hidden_states=False,
+                              output_scores=False, output_logits=False, prefill_chunk_size=None,
+                              _pad_token_tensor=torch.tensor(0), max_length=prompt.shape[1] + steps + 1,
+                              do_sample=False)
+        out = dl.active_prefix_decode_generate(Scripted(schedule, 8), prompt, logits_processor=lambda i, s: s,
+                                               stopping_criteria=StoppingCriteriaList([RowEos()]),
+                                               generation_config=cfg, decoder_attention_mask=prompt.ne(0))
+        gen = out[:, prompt.shape[1]:]
+        put(name, schedule=np.array(schedule, dtype=np.int64), generated=gen.numpy())
+        meta[name] = {"eos": 2, "pad": 0, "vocab": 8}
+
+    decode_case("ref_decode_pad", [(2, 5, 5), (7, 2, 5), (7, 7, 2)], torch.tensor(((0, 9), (8, 9), (0, 9))))
+    rs = np.random.default_rng(4242)
+    sched = rs.integers(3, 8, size=(7, 6))
+    for r in range(6):  # every row ends: an EOS at a random step, the last step for the rest
+        sched[rs.integers(0, 7) if r < 5 else 6, r] = 2
+    sched[6, :] = 2
+    decode_case("ref_decode_pad_random", [tuple(int(v) for v in row) for row in sched],
+                torch.randint(1, 8, (6, 3), generator=g))
 
     fixtures["meta.json"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
     np.savez_compressed(OUT, **fixtures)

@@ -13,7 +13,7 @@ from typing import Callable
 
 import numpy as np
 
-from . import _native as N
+from mapperatorinator_b200 import _native as N
 from .workloads import StepInputs
 
 _DTYPE_CODES = {"f32": N.DTYPE_F32, "bf16": N.DTYPE_BF16, "f16": N.DTYPE_F16}

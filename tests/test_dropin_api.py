@@ -225,26 +225,49 @@ def test_sample_entry_point_greedy_and_keep_set(cuda_device, name):
 
 
 @pytest.mark.gpu
-def test_sample_distribution_matches_multinomial(cuda_device):
-    # inverse-CDF draws from uniforms vs torch.multinomial: chi-square over 2e5 draws
+@pytest.mark.parametrize("top_k,top_p", [(0, 1.0), (20, 0.9)])
+def test_sample_distribution_matches_multinomial(cuda_device, top_k, top_p):
+    """Inverse-CDF draws from uniforms against torch.multinomial, 2^20 draws each:
+    a goodness-of-fit chi-square of our draws against the exact renormalised
+    probabilities, and a two-sample chi-square of our histogram against
+    torch.multinomial's (the reference's sampler) on the same probabilities."""
     torch.manual_seed(0)
-    logits = torch.randn(1, 64, device=cuda_device) * 1.5
-    n = 200_000
+    V = 64
+    logits = torch.randn(1, V, device=cuda_device) * 1.5
+    n = 1 << 20
     u = torch.rand(n, device=cuda_device)
-    rows = logits.expand(n, 64).contiguous()
-    ours = S._sample(rows, True, 1.0, 0, 1.0, uniforms=u).view(-1)
-    counts = torch.bincount(ours, minlength=64).double().cpu()
-    p = torch.softmax(logits.double(), -1).cpu()[0]
+    rows = logits.expand(n, V).contiguous()
+    ours = S._sample(rows, True, top_p, top_k, 1.0, uniforms=u).view(-1)
+    counts = torch.bincount(ours, minlength=V).double().cpu()
+    # the reference's probabilities: HF top-k then the _sample top-p rule, softmax
+    x = logits.double().cpu()[0]
+    if top_k:
+        x = torch.where(x < torch.topk(x, top_k).values[-1], torch.tensor(float("-inf"), dtype=x.dtype), x)
+    if top_p < 1.0:
+        sx, si = torch.sort(x, descending=True)
+        cum = torch.softmax(sx, -1).cumsum(-1)
+        rm = cum > top_p
+        rm[1:] = rm[:-1].clone()
+        rm[0] = False
+        x = x.scatter(0, si, sx.masked_fill(rm, float("-inf")))
+    p = torch.softmax(x, -1)
     expected = p * n
     mask = expected > 5
     chi2 = (((counts - expected) ** 2) / expected)[mask].sum().item()
     dof = int(mask.sum()) - 1
     assert chi2 < dof + 6 * (2 * dof) ** 0.5, (chi2, dof)
+    assert counts[p == 0].sum() == 0  # nothing outside the keep set
+    theirs = torch.bincount(torch.multinomial(p.float().to(cuda_device), n, replacement=True), minlength=V)
+    theirs = theirs.double().cpu()
+    both = (counts + theirs) > 0
+    chi2b = (((counts - theirs) ** 2) / (counts + theirs))[both].sum().item()
+    dofb = int(both.sum()) - 1
+    assert chi2b < dofb + 6 * (2 * dofb) ** 0.5, (chi2b, dofb)
 
 
 @pytest.mark.gpu
 def test_fused_sampler_public_api_matches_oracle(cuda_device):
-    from mapperatorinator_b200 import workloads as W
+    from tests.harness import workloads as W
     from oracle import oracle
 
     s = W.batched_decode(seed=5, pairs=32)
@@ -270,3 +293,26 @@ def test_fused_sampler_public_api_matches_oracle(cuda_device):
         assert np.array_equal(fs.mono_state.cpu().numpy(), ref["mono_state"])
         assert np.array_equal(fs.scores.cpu().numpy().view(np.uint32), ref["out_scores"].view(np.uint32))
         host = host.with_(mono_state=ref["mono_state"], prev_token=ref["prev_token"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["ref_decode_pad", "ref_decode_pad_random"])
+def test_fused_sampler_pads_finished_rows_like_the_reference_loop(cuda_device, name):
+    """FusedSampler(track_finished=True), greedy, against the tokens the
+    reference's active_prefix_decode_generate emits for the same scripted
+    logits: finished rows get pad 0 and the loop state follows the EOS 2."""
+    import torch
+
+    from mapperatorinator_b200.sampling import FusedSampler
+
+    c = G.case(name)
+    sched, want = c["schedule"], c["generated"]
+    steps, rows = sched.shape
+    s = FusedSampler(vocab_size=8, num_rows=rows, device=cuda_device, do_sample=False, eos_token_ids=(2,),
+                     pad_token_id=0, track_finished=True)
+    for t in range(steps):
+        x = torch.full((rows, 8), -1000.0, device=cuda_device)
+        x[torch.arange(rows), torch.from_numpy(sched[t]).to(cuda_device)] = 1000.0
+        ids = s.step(x)
+        assert torch.equal(ids.cpu(), torch.from_numpy(want[:, t])), t
+    assert not s.unfinished.any().item()

@@ -5,8 +5,8 @@ import numpy as np
 import pytest
 
 from mapperatorinator_b200 import _native as N
-from mapperatorinator_b200 import workloads as W
-from mapperatorinator_b200.stepargs import DeviceStep, fill_args, host_arrays
+from tests.harness import workloads as W
+from tests.harness.stepargs import DeviceStep, fill_args, host_arrays
 from oracle import oracle
 from tests import _golden as G
 
@@ -73,7 +73,7 @@ def test_batched_decode(cuda_device, dtype):
 
 
 def test_penalty_sweep(cuda_device):
-    s = W.penalty_sweep(seed=12, rows=512).with_(want_scores=True, want_logprobs=True)
+    s = W.penalty_sweep(seed=12, rows=1024).with_(want_scores=True, want_logprobs=True)
     assert_parity(s, cuda_device)
 
 
@@ -85,7 +85,7 @@ def test_sharded_decode_full_size(cuda_device):
 
 @pytest.mark.parametrize("vocab", [8192, 16384, 32768, 65536, 131072])
 def test_vocab_sweep_clusters(cuda_device, vocab):
-    rows = 64 if vocab <= 65536 else 16
+    rows = 256 if vocab <= 65536 else 64
     s = W.penalty_sweep(seed=vocab, rows=rows, vocab=vocab, history=256).with_(want_scores=True)
     assert_parity(s, cuda_device)
     s2 = W.batched_decode(seed=vocab + 1, pairs=rows // 2, vocab=vocab).with_(want_scores=True, want_logprobs=True)
@@ -393,3 +393,23 @@ def test_repeated_ids_count_wrap(cuda_device, ids_dtype):
                          select_mode=N.SELECT_SAMPLE, top_k=40, top_p=0.9,
                          uniforms=rng.random(rows, dtype=np.float32), want_scores=True)
         assert_parity(s, cuda_device)
+
+
+# ---------------------------------------------------------------- bounded waits
+def test_row_warp_copy_timeout_marks_every_remaining_row(cuda_device):
+    """The row-per-warp kernel's bounded wait for a staged row: with the test hook
+    the first wait of every CTA gives up at once; that row and every later row of
+    the CTA get pad_id and MTR_ROW_COPY_TIMEOUT (no row keeps an earlier token),
+    the CTA drains its copy, and the next launch is unaffected."""
+    import torch
+
+    if _kernel["name"] != "warp":
+        pytest.skip("row-per-warp kernel only")
+    s = W.penalty_sweep(seed=161, rows=4096).with_(pad_id=11)
+    dev = DeviceStep(s.with_(flags=N.FLAG_KERNEL_ROW_WARP | N.FLAG_TEST_COPY_TIMEOUT), cuda_device)
+    dev.launch()
+    torch.cuda.synchronize(cuda_device)
+    got = dev.results()
+    assert (got["out_status"] & N.ROW_COPY_TIMEOUT).all()
+    assert (got["out_ids"] == 11).all()
+    assert_parity(s, cuda_device)  # the same rows again, without the hook

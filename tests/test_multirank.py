@@ -12,7 +12,7 @@ import torch
 import torch.multiprocessing as mp
 
 from mapperatorinator_b200 import parallel
-from mapperatorinator_b200 import workloads as W
+from tests.harness import workloads as W
 
 
 def test_shard_range_partitions():

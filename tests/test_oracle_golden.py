@@ -117,3 +117,50 @@ def test_hf_repetition_penalty_then_warpers():
         kg, kr = np.isfinite(out[row]), np.isfinite(ref[row])
         if not np.array_equal(kg, kr):
             assert G.explain_keep_mismatch(c["processed"][row], kr, kg, 0.95, int(r["out_status"][row])), row
+
+
+# ---------------------------------------------------------------- the CPU port used by bench.py
+@pytest.mark.parametrize("name", ["chain_cfg_mono_temp", "chain_bias_cfg2", "chain_c0_shape", "chain_c1_bf16",
+                                  "hf_repetition"])
+def test_torch_chain_port_matches_reference(name):
+    """oracle/torch_chain.py (the CPU chain bench.py falls back to) reproduces the
+    reference's processed scores and HF-warped scores bit for bit."""
+    import torch
+
+    from oracle import torch_chain as TC
+
+    c = G.case(name)
+    m = c["meta"]
+    logits = torch.from_numpy(c["logits"].astype(np.float32))
+    ids = torch.from_numpy(c["input_ids"].astype(np.int64))
+    if name == "hf_repetition":
+        prm = TC.ChainParams(repetition_penalty=m["penalty"])
+    else:
+        prm = TC.ChainParams(cfg_scale=m["cfg"], ts_range=tuple(m["ts"]), sos_ids=tuple(m["sos"]),
+                             timeshift_bias=m["bias"], temperature=m["temps"][0])
+    got = TC.processed_scores(logits, ids, prm).numpy()
+    assert np.array_equal(got.view(np.uint32), c["processed"].view(np.uint32))
+    prm.top_k, prm.top_p = m["top_k"], m["top_p"]
+    got = TC.processed_scores(logits, ids, prm).numpy()
+    assert np.array_equal(got.view(np.uint32), c["final_hf"].view(np.uint32))
+
+
+@pytest.mark.parametrize("name", ["ref_decode_pad", "ref_decode_pad_random"])
+def test_oracle_decode_loop_pad_and_finished(name):
+    """Pad-on-finished and EOS tracking step by step, pinned to the reference's
+    own decode loop (active_prefix_decode_generate on scripted one-hot logits)."""
+    from tests.harness.workloads import StepInputs
+
+    c = G.case(name)
+    sched, want = c["schedule"], c["generated"]
+    steps, rows = sched.shape
+    unf = np.ones(rows, dtype=np.uint8)
+    for t in range(steps):
+        x = np.full((rows, 8), -1000.0, dtype=np.float32)
+        x[np.arange(rows), sched[t]] = 1000.0
+        s = StepInputs(logits=x, dtype="f32", num_rows=rows, select_mode=N.SELECT_ARGMAX, unfinished=unf,
+                       pad_id=0, eos_ids=(2,))
+        r = oracle.run(s)
+        assert np.array_equal(r["out_ids"], want[:, t]), t
+        unf = r["unfinished"]
+    assert not unf.any()
