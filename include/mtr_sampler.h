@@ -43,7 +43,7 @@
 extern "C" {
 #endif
 
-#define MTR_ABI_VERSION 1
+#define MTR_ABI_VERSION 2
 
 /* Limits (also reported by mtr_sampler_query). */
 #define MTR_MAX_VOCAB 131072
@@ -54,6 +54,7 @@ extern "C" {
 #define MTR_MAX_GRAMMAR_CLASSES 32
 #define MTR_MAX_EOS_IDS 16
 #define MTR_MAX_EOS_RANGES 2
+#define MTR_MAX_LB_EOS 8
 
 /* Return codes of every entry point. */
 typedef enum MtrStatus {
@@ -97,6 +98,12 @@ typedef enum MtrTopPMode {
   MTR_TOPP_HF = 0,       /* keep token while mass ranked strictly above it <  top_p */
   MTR_TOPP_SAMPLE_FN = 1 /* keep token while mass ranked strictly above it <= top_p */
 } MtrTopPMode;
+
+typedef enum MtrLookbackMode {
+  MTR_LOOKBACK_OFF = 0,
+  MTR_LOOKBACK_MASK = 1,   /* ids [lb_start, lb_end) -> -inf (types_first = False) */
+  MTR_LOOKBACK_RENORM = 2  /* renormalise the range away after a timed-event token (types_first = True) */
+} MtrLookbackMode;
 
 typedef enum MtrSelect {
   MTR_SELECT_NONE = 0,   /* processor only: write out_scores / out_logprobs   */
@@ -206,6 +213,24 @@ typedef struct MtrSamplerArgs {
   int32_t n_eos_ranges;
   int32_t eos_range_start[MTR_MAX_EOS_RANGES];
   int32_t eos_range_end[MTR_MAX_EOS_RANGES];
+
+  /* ---- lookback bias, applied after temperature (LookbackBiasLogitsWarper,
+   *      osuT5/osuT5/inference/logit_processors.py:122-170).  RENORM: with p the
+   *      previous step's EOS probability (lb_state[row]), P = softmax of the
+   *      scores, O = P outside [lb_start, lb_end), s = 1 / (O (1 - p) + p):
+   *      when the last input id is a timed-event token and p is not NaN, the
+   *      scores become log(P s) outside the range, log(clip((s - 1) p / (1 - p),
+   *      0, 1)) at lb_start and -inf on the rest of the range; every row's
+   *      lb_state becomes this step's EOS probability (sum of P over
+   *      lb_eos_ids, before the bias; NaN for a row with NaN / +inf scores or
+   *      none finite).  Only the row-per-CTA kernel serves lookback. ---- */
+  int32_t lookback_mode;           /* MtrLookbackMode */
+  int32_t lb_start;                /* lookback time-shift ids are [lb_start, lb_end) */
+  int32_t lb_end;
+  int32_t n_lb_eos;
+  int32_t lb_eos_ids[MTR_MAX_LB_EOS];  /* eos and context-eos ids (a repeated id counts twice) */
+  const uint32_t* lb_timed_bits;   /* [ceil(V/32)] membership bitmap of timed-event ids */
+  float* lb_state;                 /* [B] previous step's EOS probability, NaN = no previous step; rewritten */
 } MtrSamplerArgs;
 
 /* Launch geometry chosen for a problem size (diagnostics and tests). */

@@ -16,7 +16,7 @@ from pathlib import Path
 
 from . import build as _build
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_VOCAB = 131072
 MAX_IDS_LEN = 65535
 MAX_SOS_IDS = 16
@@ -25,6 +25,7 @@ MAX_COL_TEMP_RANGES = 8
 MAX_GRAMMAR_CLASSES = 32
 MAX_EOS_IDS = 16
 MAX_EOS_RANGES = 2
+MAX_LB_EOS = 8
 
 # MtrStatus
 OK = 0
@@ -51,6 +52,7 @@ MONO_OFF, MONO_STATE, MONO_SCAN = 0, 1, 2
 TEMP_SCALAR, TEMP_ROW_CONDITIONAL, TEMP_COLUMN_RANGES = 0, 1, 2
 TOPP_HF, TOPP_SAMPLE_FN = 0, 1
 SELECT_NONE, SELECT_ARGMAX, SELECT_SAMPLE = 0, 1, 2
+LOOKBACK_OFF, LOOKBACK_MASK, LOOKBACK_RENORM = 0, 1, 2
 
 FLAG_MONO_UPDATE_FROM_IDS = 1 << 0
 FLAG_MONO_UPDATE_FROM_SAMPLE = 1 << 1
@@ -124,6 +126,13 @@ class MtrSamplerArgs(ctypes.Structure):
         ("n_eos_ranges", c_int32),
         ("eos_range_start", c_int32 * MAX_EOS_RANGES),
         ("eos_range_end", c_int32 * MAX_EOS_RANGES),
+        ("lookback_mode", c_int32),
+        ("lb_start", c_int32),
+        ("lb_end", c_int32),
+        ("n_lb_eos", c_int32),
+        ("lb_eos_ids", c_int32 * MAX_LB_EOS),
+        ("lb_timed_bits", c_void_p),
+        ("lb_state", c_void_p),
     ]
 
 

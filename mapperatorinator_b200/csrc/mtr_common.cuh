@@ -106,6 +106,65 @@ __device__ __forceinline__ void expfx2(float d0, float d1, uint32_t& q0, uint32_
   q1 = (d1 >= -32.0f && s1 < 32) ? (m1 >> s1) : 0u;
 }
 
+// Natural logarithm in double precision, written for this project from the
+// series ln x = e ln2 + 2 atanh(z), z = (f - 1) / (f + 1), x = f 2^e with f in
+// [sqrt(1/2), sqrt(2)) (|z| <= 0.172, so twelve odd terms reach 2^-60).  Every
+// step is a single IEEE-rounded double operation, so the CPU oracle's copy
+// (compiled without contraction) gives the same bits.  Used by the lookback
+// bias only, a few times per row.
+__device__ __forceinline__ double log_d(double x) {
+  if (x != x) return x;
+  if (x < 0.0) return __longlong_as_double(0x7ff8000000000000LL);
+  if (x == 0.0) return __longlong_as_double((long long)0xfff0000000000000ULL);
+  if (x == __longlong_as_double(0x7ff0000000000000LL)) return x;
+  int e = 0;
+  unsigned long long b = (unsigned long long)__double_as_longlong(x);
+  if ((b >> 52) == 0ull) {  // subnormal
+    x = __dmul_rn(x, 0x1p54);
+    b = (unsigned long long)__double_as_longlong(x);
+    e = -54;
+  }
+  e += (int)(b >> 52) - 1023;
+  double f = __longlong_as_double((long long)((b & 0x000fffffffffffffull) | 0x3ff0000000000000ull));
+  if (f > 0x1.6a09e667f3bcdp+0) {
+    f = __dmul_rn(f, 0.5);
+    e += 1;
+  }
+  const double z = __ddiv_rn(__dsub_rn(f, 1.0), __dadd_rn(f, 1.0));
+  const double w = __dmul_rn(z, z);
+  double p = 0x1.642c8590b2164p-5;  // 1/23
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.8618618618618p-5);  // 1/21
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.af286bca1af28p-5);  // 1/19
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.e1e1e1e1e1e1ep-5);  // 1/17
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.1111111111111p-4);  // 1/15
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.3b13b13b13b14p-4);  // 1/13
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.745d1745d1746p-4);  // 1/11
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.c71c71c71c71cp-4);  // 1/9
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.2492492492492p-3);  // 1/7
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.999999999999ap-3);  // 1/5
+  p = __dadd_rn(__dmul_rn(p, w), 0x1.5555555555555p-2);  // 1/3
+  p = __dadd_rn(__dmul_rn(p, w), 1.0);
+  return __dadd_rn(__dmul_rn((double)e, 0x1.62e42fefa39efp-1), __dmul_rn(__dmul_rn(2.0, z), p));
+}
+
+// The lookback bias's row constants (osuT5/osuT5/inference/logit_processors.py:150-166)
+// from the fixed-point masses of the row before the bias: Q over every finite
+// score, O over the ids outside [lb_start, lb_end), the previous step's EOS
+// probability p.  s = 1 / ((O/Q)(1 - p) + p); the scores outside the range
+// become x - c with c = max + ln(Q 2^-31) - ln s (the log of the renormalised
+// probability), lb_start becomes ln(clip((s - 1) p / (1 - p), 0, 1)).
+__device__ __forceinline__ void lookback_consts(u64 Q, u64 O, float pf, float mx, double* c, float* lbv) {
+  const double p = (double)pf, pe = __dsub_rn(1.0, p);
+  const double ratio = __ddiv_rn((double)O, (double)Q);
+  const double s = __ddiv_rn(1.0, __dadd_rn(__dmul_rn(ratio, pe), p));
+  double ex = __ddiv_rn(__dmul_rn(__dsub_rn(s, 1.0), p), pe);
+  if (ex < 0.0) ex = 0.0;
+  else if (ex > 1.0) ex = 1.0;
+  const double lq = __dsub_rn(log_d((double)Q), __dmul_rn(31.0, 0x1.62e42fefa39efp-1));
+  *c = __dsub_rn(__dadd_rn((double)mx, lq), log_d(s));
+  *lbv = __double2float_rn(log_d(ex));
+}
+
 // x / t correctly rounded, given y = RN(1/t) (Markstein: q0 = x*y, r = x - q0*t
 // exactly, q = q0 + r*y).  Magnitudes outside [2^-60, 2^60) and NaN take the
 // IEEE divide; zeros and infinities pass through (t is positive and finite).

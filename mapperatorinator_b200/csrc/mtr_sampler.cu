@@ -202,6 +202,15 @@ struct alignas(16) Shared {
   StatX stat;
   u64 cta_mass;
   uint32_t cta_nfin;
+  // lookback bias (renormalising form)
+  StatX lbx;       // this CTA's maximum and non-finite flag of the scores before the bias
+  u64 lbs[3];      // this CTA's masses Q, O, E
+  double lb_c;     // scores outside the range become x - lb_c
+  float lb_v;      // the score of lb_start
+  float lb_new;    // the row's next lb_state
+  float lb_p;      // the row's lb_state on entry
+  int32_t lb_timed;  // the last input id is a timed-event token
+  int32_t lb_do;     // apply the transform
   // per-warp partials
   float wf[32];
   int32_t wi[32];
@@ -416,6 +425,16 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       }
       sm.u = u;
       sm.status_u = status;
+    } else if (warp == 5) {
+      if (a.lookback_mode == MTR_LOOKBACK_RENORM) {
+        int timed = 0;
+        if (L > 0) {
+          const int64_t t = load_id(a, row, L - 1);
+          timed = t >= 0 && t < V && ((__ldg(a.lb_timed_bits + (t >> 5)) >> (t & 31)) & 1u);
+        }
+        sm.lb_timed = timed;
+        sm.lb_p = a.lb_state[row];
+      }
     } else if (warp == 4) {
       sm.status = 0u;
       sm.n_uniq = 0;
@@ -665,6 +684,119 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     if (t != 1.0f) {
 #pragma unroll
       for (int k = 0; k < EPT; k += 2) div_by2(x[k], x[k + 1], t, y);
+    }
+  }
+
+  // ------------------------------------------------------------ lookback bias
+  // logit_processors.py:143-170.  Mask form: [lb_start, lb_end) -> -inf.
+  // Renormalising form: the row's maximum, then the fixed-point masses Q (all
+  // finite), O (outside the range) and E (the EOS ids) give the next state E/Q
+  // and, after a timed-event token with a known previous state, the shift c
+  // (lookback_consts) applied in double to the scores outside the range.
+  if (a.lookback_mode == MTR_LOOKBACK_MASK) {
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      const int id = id_of(k);
+      if (id >= a.lb_start && id < a.lb_end) x[k] = NEG;
+    }
+  } else if (a.lookback_mode == MTR_LOOKBACK_RENORM) {
+    float m0 = NEG;
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < EPT; ++k) {
+      bad |= x[k] != x[k] || x[k] == pos_inf();
+      m0 = fmaxf(m0, x[k]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m0 = fmaxf(m0, __shfl_xor_sync(FULL, m0, o));
+    bad = __any_sync(FULL, bad);
+    if (lane == 0) {
+      sm.wf[warp] = m0;
+      sm.wu2[warp] = bad;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float m = NEG;
+      uint32_t b = 0;
+      for (int w = 0; w < NW; ++w) {
+        m = fmaxf(m, sm.wf[w]);
+        b |= sm.wu2[w];
+      }
+      sm.lbx.mx = m;
+      sm.lbx.nan = b;
+    }
+    Clu<CS>::sync();
+    float m = NEG;
+    uint32_t rbad = 0;
+#pragma unroll
+    for (int r = 0; r < CS; ++r) {
+      const StatX st = *Clu<CS>::at(&sm.lbx, r);
+      m = fmaxf(m, st.mx);
+      rbad |= st.nan;
+    }
+    if (rbad || m == NEG) {  // row-uniform: the row is left as it is
+      if (tid == 0) sm.lb_new = __int_as_float(0x7fc00000);
+    } else {
+      u64 q = 0, o = 0, e = 0;
+      const int nle = a.n_lb_eos;
+#pragma unroll
+      for (int k = 0; k < EPT; ++k) {
+        if (!(x[k] > NEG)) continue;
+        const u64 qv = expfx(__fsub_rn(x[k], m));
+        const int id = id_of(k);
+        q += qv;
+        if (id < a.lb_start || id >= a.lb_end) o += qv;
+        for (int j = 0; j < nle; ++j)
+          if (a.lb_eos_ids[j] == id) e += qv;
+      }
+      q = warp_sum_u64(q);
+      o = warp_sum_u64(o);
+      e = warp_sum_u64(e);
+      if (lane == 0) {
+        sm.wl[warp * 4 + 0] = q;
+        sm.wl[warp * 4 + 1] = o;
+        sm.wl[warp * 4 + 2] = e;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        u64 t0 = 0, t1 = 0, t2 = 0;
+        for (int w = 0; w < NW; ++w) {
+          t0 += sm.wl[w * 4 + 0];
+          t1 += sm.wl[w * 4 + 1];
+          t2 += sm.wl[w * 4 + 2];
+        }
+        sm.lbs[0] = t0;
+        sm.lbs[1] = t1;
+        sm.lbs[2] = t2;
+      }
+      Clu<CS>::sync();
+      if (tid == 0) {
+        u64 Q = 0, O = 0, Em = 0;
+        for (int r = 0; r < CS; ++r) {
+          const u64* p = Clu<CS>::at(sm.lbs, r);
+          Q += p[0];
+          O += p[1];
+          Em += p[2];
+        }
+        sm.lb_new = __double2float_rn(__ddiv_rn((double)Em, (double)Q));
+        const float pf = sm.lb_p;
+        const int on = sm.lb_timed && pf == pf;
+        sm.lb_do = on;
+        if (on) lookback_consts(Q, O, pf, m, &sm.lb_c, &sm.lb_v);
+      }
+      __syncthreads();
+      if (sm.lb_do) {
+        const double c = sm.lb_c;
+        const float lv = sm.lb_v;
+#pragma unroll
+        for (int k = 0; k < EPT; ++k) {
+          const int id = id_of(k);
+          if (id >= V) continue;
+          if (id == a.lb_start) x[k] = lv;
+          else if (id > a.lb_start && id < a.lb_end) x[k] = NEG;
+          else x[k] = __double2float_rn(__dsub_rn((double)x[k], c));
+        }
+      }
     }
   }
 
@@ -1545,6 +1677,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
       if (a.out_ids) a.out_ids[row] = fin;
     }
     if (a.mono_mode != MTR_MONO_OFF && a.mono_state) a.mono_state[row] = m;
+    if (a.lookback_mode == MTR_LOOKBACK_RENORM) a.lb_state[row] = sm.lb_new;
     if (a.out_status) a.out_status[row] = gstatus;
   }
   if constexpr (CS > 1) cg::this_cluster().sync();  // no CTA leaves while its shared memory may be read
@@ -3299,6 +3432,21 @@ static int validate(const MtrSamplerArgs* a) {
   if (a->n_eos < 0 || a->n_eos > MTR_MAX_EOS_IDS) return MTR_ERR_BAD_PARAM;
   if (a->n_eos_ranges < 0 || a->n_eos_ranges > MTR_MAX_EOS_RANGES) return MTR_ERR_BAD_PARAM;
   if (a->num_rows > (1 << 24)) return MTR_ERR_BAD_SHAPE;
+  // lookback bias
+  if (a->lookback_mode < MTR_LOOKBACK_OFF || a->lookback_mode > MTR_LOOKBACK_RENORM) return MTR_ERR_BAD_PARAM;
+  if (a->lookback_mode != MTR_LOOKBACK_OFF) {
+    if (a->flags & (MTR_FLAG_KERNEL_ROW_WARP | MTR_FLAG_KERNEL_STREAM)) return MTR_ERR_UNSUPPORTED;
+    if (a->lb_start < 0 || a->lb_end < a->lb_start || a->lb_end > a->vocab) return MTR_ERR_BAD_SHAPE;
+  }
+  if (a->lookback_mode == MTR_LOOKBACK_RENORM) {
+    if (a->lb_start >= a->vocab) return MTR_ERR_BAD_SHAPE;
+    if (a->n_lb_eos < 0 || a->n_lb_eos > MTR_MAX_LB_EOS) return MTR_ERR_BAD_PARAM;
+    for (int i = 0; i < a->n_lb_eos; ++i)
+      if (a->lb_eos_ids[i] < 0 || a->lb_eos_ids[i] >= a->vocab) return MTR_ERR_BAD_PARAM;
+    if (!a->lb_state || (a->ids_len > 0 && !a->lb_timed_bits)) return MTR_ERR_NULL_ARG;
+    if ((uintptr_t)a->lb_state % 4 || (uintptr_t)a->lb_timed_bits % 4) return MTR_ERR_ALIGNMENT;
+    if (a->ids_len > 0 && !a->input_ids) return MTR_ERR_NULL_ARG;
+  }
   return MTR_OK;
 }
 
@@ -3412,6 +3560,7 @@ static int pick_kernel(const MtrSamplerArgs& a, const Derived& d, int sms) {
   if (a.flags & MTR_FLAG_KERNEL_ROW_CTA) return KERNEL_ROW_CTA;
   if (a.flags & MTR_FLAG_KERNEL_ROW_WARP) return KERNEL_ROW_WARP;
   if (a.flags & MTR_FLAG_KERNEL_STREAM) return KERNEL_STREAM;
+  if (a.lookback_mode != MTR_LOOKBACK_OFF) return KERNEL_ROW_CTA;  // the lookback bias lives in the row-per-CTA kernel
   if (a.vocab > WV_MAX && sk_supported(a, d)) return KERNEL_STREAM;
   if (a.vocab > WV_MAX || a.num_rows < 2 * (int64_t)sms) return KERNEL_ROW_CTA;
   if (d.pen_on && a.ids_len - a.penalty_start > WMAX_PEN_IDS) return KERNEL_ROW_CTA;

@@ -6,6 +6,7 @@ namespace mtr {
 
 bool sk_supported(const MtrSamplerArgs& a, const Derived& d) {
   if (a.select_mode == MTR_SELECT_ARGMAX) return false;
+  if (a.lookback_mode != MTR_LOOKBACK_OFF) return false;
   if (a.top_k < 1 || a.top_k > SK_TOPK_MAX || a.top_k >= a.vocab) return false;
   if (a.vocab % 8 != 0 || a.vocab > SK_MAX_VOCAB) return false;
   if (!d.vec_ok) return false;

@@ -10,7 +10,7 @@ library; there is no CPU path (CPU tensors raise ``ValueError``).
 ``build_logits_processor_list`` returns a list holding ONE
 :class:`FusedLogitsProcessor` that performs the whole chain -- CFG ->
 monotonic time-shift mask -> timeshift bias -> temperature (scalar or
-per-row conditional) and, optionally, the top-k / top-p warpers that
+per-row conditional) -> lookback bias and, optionally, the top-k / top-p warpers that
 ``generate()`` would append -- in a single kernel launch with no host
 synchronisation.  The individual classes run the same kernel with only their
 own stage enabled.
@@ -24,7 +24,7 @@ from typing import Iterable
 import torch
 
 from . import _native as N
-from .sampling import set_input_ids, set_logits
+from .sampling import set_input_ids, set_logits, token_bitmap
 
 try:  # the base class is only a marker; any object with __call__ works in HF lists
     from transformers import LogitsProcessor as _LogitsProcessorBase
@@ -90,14 +90,53 @@ def _sos_ids(tokenizer) -> tuple[int, ...]:
     return (int(tokenizer.sos_id),) + tuple(int(v) for v in getattr(tokenizer, "context_sos", {}).values())
 
 
+# Event types whose tokens carry a time (osuT5/osuT5/dataset/data_utils.py:60-78);
+# the lookback bias acts after one of them.  Names, so any EventType enum with
+# these member names works.
+TIMED_EVENT_NAMES = ("CIRCLE", "SPINNER", "SPINNER_END", "SLIDER_HEAD", "LAST_ANCHOR", "SLIDER_END", "BEAT",
+                     "MEASURE", "TIMING_POINT", "KIAI", "HOLD_NOTE", "HOLD_NOTE_END", "DRUMROLL", "DRUMROLL_END",
+                     "DENDEN", "DENDEN_END", "SCROLL_SPEED_CHANGE")
+
+
+def _encode_time_shift(tokenizer, value: int) -> int:
+    """tokenizer.encode(Event(TIME_SHIFT, value)) (tokenizer.py:276-290): the
+    range's first id + value - min_value, ValueError outside [min, max]."""
+    start = _event_start(tokenizer, "TIME_SHIFT")
+    if start is None:
+        raise ValueError("unknown event type: TIME_SHIFT")
+    er_table = getattr(tokenizer, "event_range", None)
+    lo, hi = 0, None
+    if er_table:
+        k = _event_key(er_table, "TIME_SHIFT")
+        if k is not None:
+            lo, hi = int(er_table[k].min_value), int(er_table[k].max_value)
+    else:
+        hi = _event_end(tokenizer, "TIME_SHIFT") - start - 1
+    if value < lo or (hi is not None and value > hi):
+        raise ValueError(f"event value {value} is not within range [{lo}, {hi}] for event type TIME_SHIFT")
+    return int(start) + value - lo
+
+
+def lookback_spec(lookback_max_time: float, tokenizer, types_first: bool) -> dict:
+    """The constants LookbackBiasLogitsWarper derives from the tokenizer
+    (logit_processors.py:127-141): the lookback time-shift ids [start, end),
+    the EOS ids (eos + every context eos) and the timed-event ids."""
+    start = int(_event_start(tokenizer, "TIME_SHIFT"))
+    end = _encode_time_shift(tokenizer, int(lookback_max_time / MILISECONDS_PER_STEP))
+    eos = (int(tokenizer.eos_id),) + tuple(int(v) for v in getattr(tokenizer, "context_eos", {}).values())
+    if len(eos) > N.MAX_LB_EOS:
+        raise ValueError(f"at most {N.MAX_LB_EOS} eos / context-eos ids")
+    timed = []
+    for name in TIMED_EVENT_NAMES:
+        k = _event_key(tokenizer.event_start, name)
+        if k is not None:
+            timed.extend(range(int(tokenizer.event_start[k]), int(tokenizer.event_end[k])))
+    return {"mode": N.LOOKBACK_RENORM if types_first else N.LOOKBACK_MASK, "start": start, "end": end,
+            "eos_ids": eos, "timed": tuple(timed)}
+
+
 def _bitmap(tokens: Iterable[int], vocab: int, device) -> torch.Tensor:
-    words = torch.zeros((vocab + 31) // 32, dtype=torch.int64)
-    for t in tokens:
-        t = int(t)
-        if 0 <= t < vocab:
-            words[t >> 5] |= 1 << (t & 31)
-    words = torch.where(words >= 2**31, words - 2**32, words)
-    return words.to(torch.int32).to(device)
+    return token_bitmap(tokens, vocab, device)
 
 
 # ---------------------------------------------------------------- the fused processor
@@ -117,7 +156,8 @@ class FusedLogitsProcessor(_LogitsProcessorBase):
                  stateful_monotonic: bool = False, timeshift_bias: float = 0.0, temperature: float = 1.0,
                  conditionals: list[tuple[float, tuple[int, ...], int]] = (), top_k: int = 0, top_p: float = 1.0,
                  top_p_mode: str = "hf", grammar=None, repetition_penalty: float = 1.0,
-                 frequency_penalty: float = 0.0, presence_penalty: float = 0.0, inplace: bool = True):
+                 frequency_penalty: float = 0.0, presence_penalty: float = 0.0, lookback: dict | None = None,
+                 inplace: bool = True):
         if cfg_scale <= 1.0 and cfg_scale != 1.0:
             cfg_scale = 1.0
         if not (temperature > 0):
@@ -143,10 +183,12 @@ class FusedLogitsProcessor(_LogitsProcessorBase):
         self.repetition_penalty = float(repetition_penalty)
         self.frequency_penalty = float(frequency_penalty)
         self.presence_penalty = float(presence_penalty)
+        self.lookback = lookback
         self.inplace = inplace
         self._bits: dict = {}
         self._state: dict = {}
         self._state_len: dict = {}
+        self._lb_state: dict = {}
 
     # per-device constant tables
     def _cond_bits(self, vocab: int, device):
@@ -155,10 +197,18 @@ class FusedLogitsProcessor(_LogitsProcessorBase):
             self._bits[key] = [_bitmap(toks, vocab, device) for _t, toks, _o in self.conditionals]
         return self._bits[key]
 
+    def _timed_bits(self, vocab: int, device):
+        key = ("timed", vocab, device)
+        if key not in self._bits:
+            self._bits[key] = _bitmap(self.lookback["timed"], vocab, device)
+        return self._bits[key]
+
     def reset(self) -> None:
-        """Forget the stateful monotonic state (the next call re-scans input_ids)."""
+        """Forget the per-row state: the stateful monotonic state (the next call
+        re-scans input_ids) and the lookback bias's previous EOS probability."""
         self._state.clear()
         self._state_len.clear()
+        self._lb_state.clear()
 
     def __call__(self, input_ids: torch.LongTensor, scores: torch.FloatTensor) -> torch.FloatTensor:
         if not scores.is_cuda:
@@ -235,6 +285,21 @@ class FusedLogitsProcessor(_LogitsProcessorBase):
         a.repetition_penalty = self.repetition_penalty
         a.frequency_penalty = self.frequency_penalty
         a.presence_penalty = self.presence_penalty
+        if self.lookback is not None:
+            lb = self.lookback
+            a.lookback_mode = lb["mode"]
+            a.lb_start, a.lb_end = lb["start"], lb["end"]
+            if lb["mode"] == N.LOOKBACK_RENORM:
+                a.n_lb_eos = len(lb["eos_ids"])
+                for i, t in enumerate(lb["eos_ids"]):
+                    a.lb_eos_ids[i] = t
+                a.lb_timed_bits = self._timed_bits(V, dev).data_ptr()
+                key = (dev, B)
+                st = self._lb_state.get(key)
+                if st is None:  # the reference's last_scores is None: no bias on the first call
+                    st = torch.full((B,), float("nan"), dtype=torch.float32, device=dev)
+                    self._lb_state[key] = st
+                a.lb_state = st.data_ptr()
         a.select_mode = N.SELECT_NONE
         a.top_k = self.top_k if self.top_k < V else 0
         a.top_p = self.top_p
@@ -323,12 +388,23 @@ class StatefulMonotonicTimeShiftLogitsProcessor(FusedLogitsProcessor):
                          stateful_monotonic=stateful_batch1)
 
 
-class LookbackBiasLogitsWarper(_LogitsProcessorBase):
-    """logit_processors.py:122-170 -- not fused yet."""
+class LookbackBiasLogitsWarper(FusedLogitsProcessor):
+    """logit_processors.py:122-170.  types_first=False: the lookback time
+    shifts [event_start[TIME_SHIFT], encode(TIME_SHIFT, lookback_max_time / 10))
+    are masked to -inf.  types_first=True: after a timed-event token the
+    probability of the lookback range is moved to EOS (the range's first id
+    carries the extra EOS mass, the rest of it is -inf), using the previous
+    call's EOS probability, which the kernel keeps per row on the device.
+    Returns a new tensor; ``scores`` is not modified."""
 
-    def __init__(self, *args, **kwargs):
-        raise NotImplementedError(
-            "LookbackBiasLogitsWarper (lookback_time > 0) is not available in the fused sampler yet")
+    def __init__(self, lookback_max_time: float, tokenizer, types_first: bool, device=None):
+        spec = lookback_spec(lookback_max_time, tokenizer, types_first)
+        self.types_first = types_first
+        self.lookback_start = spec["start"]
+        self.lookback_end = spec["end"]
+        self.eos_ids = spec["eos_ids"]
+        self.timed_tokens = spec["timed"]
+        super().__init__(lookback=spec, inplace=False)
 
 
 # ---------------------------------------------------------------- list builders
@@ -364,8 +440,6 @@ def build_logits_processor_list(tokenizer, *, cfg_scale: float = 1.0, timeshift_
     policy follows ``monotonic_processor_factory``: the stateful factory keeps
     per-row state on the device, the default re-scans input_ids each step.
     """
-    if lookback_time > 0:
-        raise NotImplementedError("lookback_time > 0 (LookbackBiasLogitsWarper) is not fused yet")
     if not isinstance(temperature, float) and not isinstance(temperature, int):
         raise ValueError(f"`temperature` (={temperature}) has to be a strictly positive float")
     timing_temperature = temperature if timing_temperature is None else timing_temperature
@@ -385,7 +459,8 @@ def build_logits_processor_list(tokenizer, *, cfg_scale: float = 1.0, timeshift_
     proc = FusedLogitsProcessor(
         cfg_scale=cfg_scale, time_shift_range=_time_shift_range(tokenizer), sos_ids=_sos_ids(tokenizer),
         stateful_monotonic=stateful, timeshift_bias=timeshift_bias, temperature=float(temperature),
-        conditionals=conditionals, top_k=top_k, top_p=top_p, top_p_mode=top_p_mode)
+        conditionals=conditionals, top_k=top_k, top_p=top_p, top_p_mode=top_p_mode,
+        lookback=lookback_spec(lookback_time, tokenizer, types_first) if lookback_time > 0 else None)
     lst = _list_type()()
     lst.append(proc)
     return lst

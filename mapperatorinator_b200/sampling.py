@@ -71,6 +71,17 @@ def set_input_ids(args: N.MtrSamplerArgs, input_ids: torch.Tensor | None) -> Non
     args.ids_row_stride = input_ids.stride(0) if input_ids.shape[1] else 0
 
 
+def token_bitmap(tokens, vocab: int, device) -> torch.Tensor:
+    """int32 [ceil(vocab / 32)] membership bitmap: bit t & 31 of word t >> 5."""
+    words = torch.zeros((vocab + 31) // 32, dtype=torch.int64)
+    for t in tokens:
+        t = int(t)
+        if 0 <= t < vocab:
+            words[t >> 5] |= 1 << (t & 31)
+    words = torch.where(words >= 2**31, words - 2**32, words)
+    return words.to(torch.int32).to(device)
+
+
 def _uniforms(n: int, device, uniforms, generator) -> torch.Tensor:
     if uniforms is None:
         return torch.rand(n, device=device, generator=generator, dtype=torch.float32)
@@ -159,8 +170,9 @@ class FusedSampler:
 
     Chain order: CFG -> monotonic time-shift mask -> timeshift bias -> grammar
     mask -> repetition / frequency / presence penalties -> temperature ->
-    top-k -> top-p -> draw.  Device state per row: last time-shift value
-    (monotonic mask), previous token (grammar), unfinished flag.
+    lookback bias -> top-k -> top-p -> draw.  Device state per row: last
+    time-shift value (monotonic mask), previous token (grammar), unfinished
+    flag, previous EOS probability (lookback bias).
     """
 
     def __init__(self, *, vocab_size: int, num_rows: int, device, cfg_scale: float = 1.0,
@@ -173,7 +185,7 @@ class FusedSampler:
                  top_k: int = 0, top_p: float = 1.0, top_p_mode: str = "hf", do_sample: bool = True,
                  eos_token_ids: Sequence[int] = (), eos_ranges: Sequence[tuple[int, int]] = (),
                  pad_token_id: int = 0, track_finished: bool = False,
-                 return_scores: bool = False, return_logprobs: bool = False):
+                 return_scores: bool = False, return_logprobs: bool = False, lookback: dict | None = None):
         self.device = torch.device(device)
         self.vocab_size = int(vocab_size)
         self.num_rows = int(num_rows)
@@ -254,6 +266,23 @@ class FusedSampler:
         a.n_eos_ranges = len(eos_ranges)
         for i, (s, e) in enumerate(eos_ranges):
             a.eos_range_start[i], a.eos_range_end[i] = int(s), int(e)
+        # lookback bias (logit_processors.lookback_spec): previous EOS probability per row
+        self.lb_state = torch.full((B,), float("nan"), dtype=torch.float32, device=self.device)
+        self._keep_lb = None
+        if lookback is not None:
+            a.lookback_mode = int(lookback["mode"])
+            a.lb_start, a.lb_end = int(lookback["start"]), int(lookback["end"])
+            if a.lookback_mode == N.LOOKBACK_RENORM:
+                eos = tuple(lookback["eos_ids"])
+                if len(eos) > N.MAX_LB_EOS:
+                    raise ValueError(f"at most {N.MAX_LB_EOS} lookback eos ids")
+                a.n_lb_eos = len(eos)
+                for i, t in enumerate(eos):
+                    a.lb_eos_ids[i] = int(t)
+                words = token_bitmap(lookback["timed"], V, self.device)
+                self._keep_lb = words
+                a.lb_timed_bits = words.data_ptr()
+                a.lb_state = self.lb_state.data_ptr()
         self._base = a
         self._scan_next = time_shift_range is not None
         self._prev_from_ids_next = grammar is not None
@@ -263,6 +292,7 @@ class FusedSampler:
         self.mono_state.fill_(-1)
         self.prev_token.fill_(-1)
         self.unfinished.fill_(1)
+        self.lb_state.fill_(float("nan"))
         self._scan_next = self._base.mono_mode != N.MONO_OFF
         self._prev_from_ids_next = self.grammar is not None
 
@@ -276,6 +306,8 @@ class FusedSampler:
         if rows != (2 * self.num_rows if a.cfg_enabled else self.num_rows):
             raise ValueError(f"expected {2 * self.num_rows if a.cfg_enabled else self.num_rows} logits rows, got {rows}")
         set_input_ids(a, input_ids)
+        if a.lookback_mode == N.LOOKBACK_RENORM and input_ids is None:
+            raise ValueError("the lookback bias reads the last input id: pass input_ids every step")
         if input_ids is not None and input_ids.shape[0] != self.num_rows:
             raise ValueError("input_ids must have one row per output row")
         if self._scan_next and input_ids is not None:

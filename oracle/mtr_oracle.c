@@ -27,7 +27,11 @@
  *   temperature    scores / T, IEEE division with T rounded to fp32
  *                  (logits_process.py:297-301; per-row conditional form:
  *                  logit_processors.py:75-119, first match in list order)
- *   top-k          remove scores < k-th largest score (ties kept)
+ *   lookback       LookbackBiasLogitsWarper (logit_processors.py:122-170):
+ *                  types_first = False masks [lb_start, lb_end); True
+ *                  renormalises away that range after a timed-event token
+ *                  (lookback_renorm below)
+ *   top-k         remove scores < k-th largest score (ties kept)
  *                  (logits_process.py:581-588)
  *   top-p          nucleus over probabilities, see below
  *                  (logits_process.py:521-535 and compiled_decode.py:1147-1155)
@@ -183,6 +187,102 @@ static int cmp_float_desc(const void* pa, const void* pb) {
 
 static const float NEG_INF = -INFINITY;
 
+/* ln x in double: x = f 2^e with f in [sqrt(1/2), sqrt(2)), ln x = e ln2 +
+ * 2 atanh(z), z = (f - 1) / (f + 1), atanh by its odd series to z^23 (|z| <=
+ * 0.172).  Each step is one IEEE double operation (no contraction), the same
+ * sequence the kernel runs.  Exported for the CPU tests. */
+double mtr_oracle_log_d(double x) {
+  static const double C[12] = {
+      1.0,
+      0x1.5555555555555p-2, 0x1.999999999999ap-3, 0x1.2492492492492p-3, 0x1.c71c71c71c71cp-4,
+      0x1.745d1745d1746p-4, 0x1.3b13b13b13b14p-4, 0x1.1111111111111p-4, 0x1.e1e1e1e1e1e1ep-5,
+      0x1.af286bca1af28p-5, 0x1.8618618618618p-5, 0x1.642c8590b2164p-5,
+  };
+  if (x != x) return x;
+  if (x < 0.0) return NAN;
+  if (x == 0.0) return -INFINITY;
+  if (x == INFINITY) return x;
+  int e = 0;
+  uint64_t b;
+  memcpy(&b, &x, 8);
+  if ((b >> 52) == 0) {
+    x = x * 0x1p54;
+    memcpy(&b, &x, 8);
+    e = -54;
+  }
+  e += (int)(b >> 52) - 1023;
+  b = (b & 0x000fffffffffffffULL) | 0x3ff0000000000000ULL;
+  double f;
+  memcpy(&f, &b, 8);
+  if (f > 0x1.6a09e667f3bcdp+0) {
+    f = f * 0.5;
+    e += 1;
+  }
+  double z = (f - 1.0) / (f + 1.0);
+  double w = z * z;
+  double p = C[11];
+  for (int k = 10; k >= 0; --k) p = p * w + C[k];
+  return (double)e * 0x1.62e42fefa39efp-1 + (2.0 * z) * p;
+}
+
+/* LookbackBiasLogitsWarper, types_first = True
+ * (osuT5/osuT5/inference/logit_processors.py:143-170), on one row of scores
+ * after temperature.  p = the previous step's EOS probability (lb_state, NaN:
+ * no previous step), masses in fixed point: Q over every finite score, O over
+ * the ids outside [lb_start, lb_end), E over the EOS ids (a repeated id counts
+ * each time, as the reference's index-and-sum does).  When the last input id
+ * is a timed-event token and p is known:
+ *   s = 1 / ((O/Q)(1 - p) + p)
+ *   x -> x - c, c = max + ln(Q 2^-31) - ln s        outside the range
+ *   x -> -inf                                       inside the range
+ *   x[lb_start] = ln(clip((s - 1) p / (1 - p), 0, 1))
+ * The row's new state is E / Q of the scores BEFORE the transform (the
+ * reference keeps last_scores = its input); a row with NaN or +inf scores, or
+ * all -inf, stores NaN and is left as it is. */
+static void lookback_renorm(const MtrSamplerArgs* a, int64_t r, int32_t L, float* xs, int32_t V) {
+  float m = NEG_INF;
+  int bad = 0;
+  for (int32_t v = 0; v < V; ++v) {
+    float x = xs[v];
+    if (x != x || x == INFINITY) bad = 1;
+    else if (x > m) m = x;
+  }
+  const float p_prev = a->lb_state[r];
+  if (bad || m == NEG_INF) {
+    a->lb_state[r] = NAN;
+    return;
+  }
+  uint64_t Q = 0, O = 0, E = 0;
+  for (int32_t v = 0; v < V; ++v) {
+    if (!(xs[v] > NEG_INF)) continue;
+    uint32_t q = mtr_oracle_expfx(xs[v] - m);
+    Q += q;
+    if (v < a->lb_start || v >= a->lb_end) O += q;
+  }
+  for (int k = 0; k < a->n_lb_eos; ++k) {
+    int32_t id = a->lb_eos_ids[k];
+    if (xs[id] > NEG_INF) E += mtr_oracle_expfx(xs[id] - m);
+  }
+  a->lb_state[r] = (float)((double)E / (double)Q);
+  int timed = 0;
+  if (L > 0) {
+    int64_t t = load_id(a, r, L - 1);
+    timed = t >= 0 && t < V && ((a->lb_timed_bits[t >> 5] >> (t & 31)) & 1u);
+  }
+  if (!timed || p_prev != p_prev) return;
+  const double p = (double)p_prev, pe = 1.0 - p;
+  const double ratio = (double)O / (double)Q;
+  const double s = 1.0 / (ratio * pe + p);
+  double ex = (s - 1.0) * p / pe;
+  if (ex < 0.0) ex = 0.0;
+  else if (ex > 1.0) ex = 1.0;
+  const double lq = mtr_oracle_log_d((double)Q) - 31.0 * 0x1.62e42fefa39efp-1;
+  const double c = ((double)m + lq) - mtr_oracle_log_d(s);
+  for (int32_t v = 0; v < V; ++v)
+    xs[v] = (v >= a->lb_start && v < a->lb_end) ? NEG_INF : (float)((double)xs[v] - c);
+  xs[a->lb_start] = (float)mtr_oracle_log_d(ex);
+}
+
 /* sizeof(MtrSamplerArgs) this oracle was compiled with (layout check). */
 size_t mtr_oracle_args_size(void) { return sizeof(MtrSamplerArgs); }
 
@@ -304,6 +404,13 @@ int mtr_oracle_run(const MtrSamplerArgs* a) {
       }
       if (t != 1.0f) x = x / t;
       xs[v] = x;
+    }
+
+    /* ---- lookback bias (logit_processors.py:143-170) ---- */
+    if (a->lookback_mode == MTR_LOOKBACK_MASK) {
+      for (int32_t v = a->lb_start; v < a->lb_end && v < V; ++v) xs[v] = NEG_INF;
+    } else if (a->lookback_mode == MTR_LOOKBACK_RENORM) {
+      lookback_renorm(a, r, L, xs, V);
     }
 
     /* ---- row statistics ---- */

@@ -52,12 +52,18 @@ def load() -> ctypes.CDLL:
         lib.mtr_oracle_expfx.argtypes = [ctypes.c_float]
         lib.mtr_oracle_markstein_div.restype = ctypes.c_float
         lib.mtr_oracle_markstein_div.argtypes = [ctypes.c_float, ctypes.c_float]
+        lib.mtr_oracle_log_d.restype = ctypes.c_double
+        lib.mtr_oracle_log_d.argtypes = [ctypes.c_double]
         _lib = lib
     return _lib
 
 
 def expfx(d: float) -> int:
     return int(load().mtr_oracle_expfx(ctypes.c_float(d)))
+
+
+def log_d(x: float) -> float:
+    return float(load().mtr_oracle_log_d(ctypes.c_double(x)))
 
 
 def markstein_div(x: float, t: float) -> float:
@@ -103,6 +109,13 @@ def compare(ref: dict, got: dict, *, lp_rtol: float = 1e-5, lp_atol: float = 1e-
                 bad = np.nonzero(ref[k] != got[k])[0]
                 errs.append(f"{k}: {len(bad)} rows differ, first {bad[:5].tolist()} "
                             f"ref {ref[k][bad[:5]].tolist()} got {got[k][bad[:5]].tolist()}")
+    if "lb_state" in ref:
+        r, g = ref["lb_state"], got["lb_state"]
+        same = (r.view(np.uint32) == g.view(np.uint32)) | (np.isnan(r) & np.isnan(g))
+        if not same.all():
+            bad = np.nonzero(~same)[0]
+            errs.append(f"lb_state: {len(bad)} rows differ, first {bad[:5].tolist()} "
+                        f"ref {r[bad[:5]].tolist()} got {g[bad[:5]].tolist()}")
     if "out_scores" in ref:
         r, g = ref["out_scores"], got["out_scores"]
         same = (r.view(np.uint32) == g.view(np.uint32)) | (np.isnan(r) & np.isnan(g))

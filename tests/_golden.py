@@ -105,3 +105,72 @@ def explain_keep_mismatch(scores: np.ndarray, ref_keep: np.ndarray, got_keep: np
     diff = np.nonzero(ref_keep != got_keep)[0]
     pos = {int(t): i for i, t in enumerate(ids[order])}
     return all(abs(above[pos[int(t)]] - top_p) < margin for t in diff if int(t) in pos)
+
+
+LOOKBACK_CASES = ("lookback_renorm", "lookback_mask", "lookback_chain")
+
+
+def lookback_tokenizer(meta: dict):
+    """A duck-typed tokenizer with the event layout a lookback fixture was made with."""
+    import enum
+    from types import SimpleNamespace
+
+    et = enum.Enum("EventType", ["TIME_SHIFT"] + list(meta["extra"]))
+    ts0, ts1 = meta["ts"]
+    return SimpleNamespace(
+        sos_id=1, context_sos={}, eos_id=meta["eos"][0], context_eos={i: e for i, e in enumerate(meta["eos"][1:])},
+        event_start={et.TIME_SHIFT: ts0, **{et[k]: v[0] for k, v in meta["extra"].items()}},
+        event_end={et.TIME_SHIFT: ts1, **{et[k]: v[1] for k, v in meta["extra"].items()}},
+        event_range={et.TIME_SHIFT: SimpleNamespace(min_value=meta["ts_min"],
+                                                    max_value=meta["ts_min"] + ts1 - ts0 - 1)},
+        vocab_size_out=meta["vocab"])
+
+
+def lookback_step(name: str, t: int, lb_state: np.ndarray, **kw) -> StepInputs:
+    """Step t of a lookback fixture (processor output only), carrying lb_state."""
+    from mapperatorinator_b200.logit_processors import lookback_spec
+
+    c = case(name)
+    m = c["meta"]
+    V = m["vocab"]
+    spec = lookback_spec(m["lookback_time"], lookback_tokenizer(m), m["types_first"])
+    ids = np.ascontiguousarray(c["input_ids"][:, : m["prefix"] + t + 1].astype(np.int64))
+    B = ids.shape[0]
+    base = dict(dtype="f32", num_rows=B, input_ids=ids, select_mode=N.SELECT_NONE, want_scores=True,
+                uniforms=np.zeros(B, dtype=np.float32), lookback_mode=spec["mode"], lb_start=spec["start"],
+                lb_end=spec["end"], lb_eos_ids=spec["eos_ids"], lb_timed_bits=bits_for(spec["timed"], V),
+                lb_state=lb_state)
+    if name == "lookback_chain":
+        base.update(logits=c["logits"][t], cfg_scale=m["cfg"], mono_mode=N.MONO_SCAN, ts_start=m["ts"][0],
+                    ts_end=m["ts"][1], sos_ids=tuple(m["sos"]), timeshift_bias=m["bias"],
+                    temp_mode=N.TEMP_ROW_CONDITIONAL, temperature=m["temps"][0], cond=conditionals(m, V))
+    else:
+        base.update(logits=c["scores"][t])
+    base.update(kw)
+    return StepInputs(**base)
+
+
+def lookback_reference(name: str, t: int) -> np.ndarray:
+    c = case(name)
+    return c["out"][t] if "out" in c else c["processed"][t]
+
+
+def lookback_close(got: np.ndarray, ref: np.ndarray, lb_start: int, atol: float = 1e-5, rtol: float = 1e-6,
+                   patol: float = 1e-6) -> list:
+    """Elements where the fixed-point / double lookback transform and the
+    reference's float32 softmax-and-log disagree: -inf must match exactly,
+    finite log-probabilities within atol + rtol |ref|.  The lb_start column is
+    log((s - 1) p / (1 - p)), a difference of nearly equal float32 numbers in
+    the reference (absolute error ~1e-7 in probability), so it is compared as a
+    probability: |e^got - e^ref| <= patol."""
+    got = got.astype(np.float64)
+    ref = ref.astype(np.float64)
+    cols = np.ones(ref.shape[1], dtype=bool)
+    cols[lb_start] = False
+    g, r = got[:, cols], ref[:, cols]
+    bad = np.zeros(ref.shape, dtype=bool)
+    with np.errstate(invalid="ignore"):
+        b = (np.isneginf(r) != np.isneginf(g)) | (np.isfinite(r) & ~(np.abs(g - r) <= atol + rtol * np.abs(r)))
+        bad[:, cols] = b
+        bad[:, lb_start] = ~(np.abs(np.exp(got[:, lb_start]) - np.exp(ref[:, lb_start])) <= patol)
+    return np.argwhere(bad).tolist()

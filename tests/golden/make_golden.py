@@ -276,6 +276,61 @@ def main() -> None:
     decode_case("ref_decode_pad_random", [tuple(int(v) for v in row) for row in sched],
                 torch.randint(1, 8, (6, 3), generator=g))
 
+    # ---- lookback bias over consecutive calls (LookbackBiasLogitsWarper keeps the
+    # previous call's scores): seeded scores with EOS ids boosted per row, some
+    # masked ids, and a last input token that is a timed event on about half the
+    # rows.  TIME_SHIFT's values start at -20 (tokenizer.py:54 uses -512), so the
+    # lookback range is [16, 16 + 20 + 30).  Also the full chain with lookback. ----
+    gl = torch.Generator().manual_seed(777)
+    lb_extra = {"CIRCLE": (140, 141), "BEAT": (130, 131), "MEASURE": (131, 132), "TIMING_POINT": (132, 133),
+                "SLIDER_HEAD": (143, 150), "HOLD_NOTE": (141, 142), "HOLD_NOTE_END": (142, 143),
+                "SCROLL_SPEED": (150, 170)}
+    lb_tok = make_tokenizer(ev, ts=(16, 116), sos=1, extra=lb_extra,
+                            context_eos={ev.ContextType.TIMING: 4, ev.ContextType.KIAI: 5}, ts_min=-20, vocab=256)
+    lb_meta = {"ts": [16, 116], "ts_min": -20, "lookback_time": 300.0, "eos": [2, 4, 5],
+               "extra": {k: list(v) for k, v in lb_extra.items()}, "vocab": 256}
+
+    def lb_history(B, T):
+        ids = torch.randint(0, 256, (B, 4 + T), generator=gl)
+        timed = torch.tensor([140, 130, 131, 145, 149, 141])
+        untimed = torch.tensor([20, 60, 200, 3, 115, 170])
+        pick = torch.rand((B, T), generator=gl) < 0.5
+        ti = timed[torch.randint(0, len(timed), (B, T), generator=gl)]
+        ui = untimed[torch.randint(0, len(untimed), (B, T), generator=gl)]
+        ids[:, 4:] = torch.where(pick, ti, ui)
+        return ids
+
+    def lb_scores(R):
+        x = torch.randn((R, 256), generator=gl) * 1.5
+        x[:, [2, 4, 5]] += torch.rand((R, 1), generator=gl) * 6.0 - 2.0
+        x[: R // 2, 20:28] = -float("inf")
+        return x
+
+    for name, types_first in (("lookback_renorm", True), ("lookback_mask", False)):
+        B, T = 6, 6
+        ids = lb_history(B, T)
+        w = lp.LookbackBiasLogitsWarper(300.0, lb_tok, types_first, "cpu")
+        xs, outs = [], []
+        for t in range(T):
+            x = lb_scores(B)
+            outs.append(w(ids[:, : 4 + t + 1].clone(), x.clone()).numpy())
+            xs.append(x.numpy())
+        put(name, input_ids=ids.numpy(), scores=np.stack(xs), out=np.stack(outs))
+        meta[name] = dict(lb_meta, types_first=types_first, steps=T, prefix=4)
+
+    B, T = 4, 5
+    ids = lb_history(B, T)
+    procs = lp.build_logits_processor_list(lb_tok, cfg_scale=1.5, timeshift_bias=0.25, types_first=True,
+                                           temperature=0.9, timing_temperature=0.8, lookback_time=300.0)
+    xs, outs = [], []
+    for t in range(T):
+        x = lb_scores(2 * B)
+        outs.append(procs(ids[:, : 4 + t + 1].clone(), x.clone()).numpy())
+        xs.append(x.numpy())
+    put("lookback_chain", input_ids=ids.numpy(), logits=np.stack(xs), processed=np.stack(outs))
+    meta["lookback_chain"] = dict(lb_meta, types_first=True, steps=T, prefix=4, cfg=1.5, bias=0.25,
+                                  temps=[0.9, 0.8, 0.9, 0.9], sos=[1])
+
     fixtures["meta.json"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
     np.savez_compressed(OUT, **fixtures)
     print(f"wrote {OUT} ({OUT.stat().st_size} bytes, {len(fixtures)} arrays)")

@@ -93,6 +93,16 @@ def fill_args(args: N.MtrSamplerArgs, s: StepInputs, addr: Callable[[str], int],
     for i, (a, b) in enumerate(s.eos_ranges):
         args.eos_range_start[i] = int(a)
         args.eos_range_end[i] = int(b)
+    args.lookback_mode = int(s.lookback_mode)
+    args.lb_start = int(s.lb_start)
+    args.lb_end = int(s.lb_end)
+    if len(s.lb_eos_ids) > N.MAX_LB_EOS:
+        raise ValueError("too many lookback eos ids")
+    args.n_lb_eos = len(s.lb_eos_ids)
+    for i, t in enumerate(s.lb_eos_ids):
+        args.lb_eos_ids[i] = int(t)
+    args.lb_timed_bits = addr("lb_timed_bits")
+    args.lb_state = addr("lb_state")
     return args
 
 
@@ -133,6 +143,10 @@ def host_arrays(s: StepInputs) -> dict:
         arr["uniforms"] = np.ascontiguousarray(s.uniforms, dtype=np.float32)
     if s.unfinished is not None:
         arr["unfinished"] = np.array(s.unfinished, dtype=np.uint8, copy=True)
+    if s.lb_timed_bits is not None:
+        arr["lb_timed_bits"] = np.ascontiguousarray(s.lb_timed_bits, dtype=np.uint32)
+    if s.lb_state is not None:
+        arr["lb_state"] = np.array(s.lb_state, dtype=np.float32, copy=True)
     arr["out_ids"] = np.full(B, -7, dtype=np.int64)
     arr["out_status"] = np.full(B, 0xFFFFFFFF, dtype=np.uint32)
     if s.want_scores:
@@ -142,7 +156,8 @@ def host_arrays(s: StepInputs) -> dict:
     return arr
 
 
-STATE_KEYS = ("out_ids", "out_status", "out_scores", "out_logprobs", "mono_state", "prev_token", "unfinished")
+STATE_KEYS = ("out_ids", "out_status", "out_scores", "out_logprobs", "mono_state", "prev_token", "unfinished",
+              "lb_state")
 
 
 class DeviceStep:

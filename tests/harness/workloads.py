@@ -89,6 +89,13 @@ class StepInputs:
     pad_id: int = 0
     eos_ids: tuple = ()
     eos_ranges: tuple = ()
+    # lookback bias (0 off, 1 mask, 2 renormalise)
+    lookback_mode: int = 0
+    lb_start: int = 0
+    lb_end: int = 0
+    lb_eos_ids: tuple = ()
+    lb_timed_bits: np.ndarray | None = None  # [ceil(V/32)] uint32
+    lb_state: np.ndarray | None = None       # [B] float32, NaN = no previous step
 
     @property
     def vocab(self) -> int:
@@ -190,3 +197,37 @@ WORKLOADS = {
     "penalty_sweep": penalty_sweep,
     "sharded_decode": sharded_decode,
 }
+
+
+def lookback_decode(seed: int = 7, pairs: int = 64, vocab: int = 4096, dtype: str = "bf16", step: int = 0,
+                    lb_state: np.ndarray | None = None) -> StepInputs:
+    """A sampling step with the lookback bias renormalising (types_first=True):
+    CFG pairs, monotonic state, lookback range [100, 600), EOS ids (2, 7, 9)
+    boosted per row, timed-event ids = a seeded 1/8 of the vocabulary, last
+    input id timed on about half the rows.  `step` reseeds the scores and last
+    ids; `lb_state` carries the previous step's EOS probabilities (default: a
+    mix of NaN and values in [0, 0.9])."""
+    rng = np.random.default_rng(seed)
+    timed = np.sort(rng.choice(vocab, size=max(vocab // 8, 1), replace=False))
+    untimed = np.setdiff1d(np.arange(vocab), timed)
+    bits = np.zeros((vocab + 31) // 32, dtype=np.uint32)
+    np.bitwise_or.at(bits, timed >> 5, (np.uint32(1) << (timed & 31).astype(np.uint32)))
+    if lb_state is None:
+        lb_state = rng.uniform(0.0, 0.9, size=pairs).astype(np.float32)
+        lb_state[rng.random(pairs) < 0.2] = np.nan
+    rs = np.random.default_rng(seed * 1000 + step + 1)
+    x = _spiky_rows(rs, 2 * pairs, vocab, 1.5)
+    x[:, [2, 7, 9]] += rs.uniform(-2.0, 5.0, size=(2 * pairs, 1)).astype(np.float32)
+    ids = rs.integers(0, vocab, size=(pairs, 6)).astype(np.int64)
+    pick = rs.random(pairs) < 0.5
+    ids[:, -1] = np.where(pick, rs.choice(timed, size=pairs), rs.choice(untimed, size=pairs))
+    lb_end = min(600, vocab)
+    ts_end = min(TS_END_4096, vocab)
+    return StepInputs(
+        logits=bf16_bits(x) if dtype == "bf16" else x.astype(np.float16) if dtype == "f16" else x, dtype=dtype,
+        num_rows=pairs, cfg_scale=1.5, input_ids=ids,
+        mono_mode=1, ts_start=0, ts_end=ts_end, sos_ids=SOS_IDS_4096,
+        mono_state=rs.integers(0, 64, size=pairs).astype(np.int32), temperature=0.9,
+        select_mode=2, top_k=40, top_p=0.9, top_p_mode=0, uniforms=rs.random(pairs, dtype=np.float32),
+        lookback_mode=2, lb_start=min(100, vocab - 1), lb_end=lb_end, lb_eos_ids=(2, 7, 9), lb_timed_bits=bits,
+        lb_state=lb_state)

@@ -218,3 +218,55 @@ def test_status_strings(lib):
     assert N.status_string(N.ERR_ABI) == "MTR_ERR_ABI"
     with pytest.raises(ValueError):
         N.check(N.ERR_BAD_PARAM)
+
+
+def _lookback_args():
+    a = _valid_args()
+    a.lookback_mode = N.LOOKBACK_RENORM
+    a.lb_start, a.lb_end = 100, 600
+    a.n_lb_eos = 2
+    a.lb_eos_ids[0], a.lb_eos_ids[1] = 2, 3
+    a.lb_state = 0x60000
+    a.lb_timed_bits = 0x70000
+    a.input_ids, a.ids_len, a.ids_row_stride, a.ids_dtype = 0x80000, 4, 4, N.IDS_I64
+    return a
+
+
+def test_lookback_validation_and_kernel(lib):
+    a = _lookback_args()
+    assert N.validate(a) == N.OK
+    # the lookback bias is served by the row-per-CTA kernel only
+    a.num_rows, a.top_k = 4096, 50
+    assert N.query_args(a).kernel == N.KERNEL_ROW_CTA
+    a.vocab = a.logits_row_stride = 65536
+    assert N.query_args(a).kernel == N.KERNEL_ROW_CTA
+    for flag in (N.FLAG_KERNEL_ROW_WARP, N.FLAG_KERNEL_STREAM):
+        b = _lookback_args()
+        b.flags = flag
+        b.top_k = 50
+        assert N.validate(b) == N.ERR_UNSUPPORTED
+    b = _lookback_args()
+    b.lookback_mode = N.LOOKBACK_MASK
+    b.flags = N.FLAG_KERNEL_ROW_WARP
+    assert N.validate(b) == N.ERR_UNSUPPORTED
+    cases = [("lookback_mode", 3, N.ERR_BAD_PARAM), ("lb_start", -1, N.ERR_BAD_SHAPE),
+             ("lb_end", 50, N.ERR_BAD_SHAPE), ("lb_end", 5000, N.ERR_BAD_SHAPE), ("n_lb_eos", 9, N.ERR_BAD_PARAM),
+             ("lb_state", 0, N.ERR_NULL_ARG), ("lb_state", 0x60002, N.ERR_ALIGNMENT),
+             ("lb_timed_bits", 0, N.ERR_NULL_ARG), ("input_ids", 0, N.ERR_NULL_ARG)]
+    for field, value, code in cases:
+        b = _lookback_args()
+        setattr(b, field, value)
+        assert N.validate(b) == code, field
+    b = _lookback_args()
+    b.lb_eos_ids[1] = 4096
+    assert N.validate(b) == N.ERR_BAD_PARAM
+    b = _lookback_args()
+    b.lb_start = b.lb_end = 4096  # the renormalising form writes lb_start: it must be an id
+    assert N.validate(b) == N.ERR_BAD_SHAPE
+    b.lookback_mode = N.LOOKBACK_MASK  # an empty mask range at the end is fine
+    assert N.validate(b) == N.OK
+    b = _lookback_args()
+    b.ids_len = b.ids_row_stride = 0
+    b.input_ids = 0
+    b.lb_timed_bits = 0  # no history: no last token to look up
+    assert N.validate(b) == N.OK

@@ -42,9 +42,14 @@ def test_rejects_optimized_stateful_mode():
         LP.MonotonicTimeShiftLogitsProcessor(_FakeTokenizer(), stateful_batch1=True)
 
 
-def test_lookback_bias_not_fused_yet():
-    with pytest.raises(NotImplementedError):
-        LP.build_logits_processor_list(_FakeTokenizer(), lookback_time=100.0)
+def test_lookback_warper_constructs_from_tokenizer():
+    m = G.case("lookback_renorm")["meta"]
+    w = LP.LookbackBiasLogitsWarper(m["lookback_time"], G.lookback_tokenizer(m), True, "cpu")
+    assert (w.lookback_start, w.lookback_end, w.eos_ids) == (16, 66, (2, 4, 5))
+    lst = LP.build_logits_processor_list(G.lookback_tokenizer(m), types_first=False, lookback_time=100.0)
+    assert lst[0].lookback["mode"] == N.LOOKBACK_MASK and lst[0].lookback["end"] == 16 + 20 + 10
+    with pytest.raises(ValueError):
+        LP.LookbackBiasLogitsWarper(5000.0, G.lookback_tokenizer(m), True, "cpu")
 
 
 def test_token_helpers():
@@ -316,3 +321,67 @@ def test_fused_sampler_pads_finished_rows_like_the_reference_loop(cuda_device, n
         ids = s.step(x)
         assert torch.equal(ids.cpu(), torch.from_numpy(want[:, t])), t
     assert not s.unfinished.any().item()
+
+
+# ---------------------------------------------------------------- GPU: lookback bias
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["lookback_renorm", "lookback_mask"])
+def test_lookback_warper_matches_reference(cuda_device, name):
+    c = G.case(name)
+    m = c["meta"]
+    w = LP.LookbackBiasLogitsWarper(m["lookback_time"], G.lookback_tokenizer(m), m["types_first"], cuda_device)
+    for t in range(m["steps"]):
+        ids = torch.from_numpy(c["input_ids"][:, : m["prefix"] + t + 1]).to(cuda_device)
+        x = torch.from_numpy(c["scores"][t]).to(cuda_device)
+        x0 = x.clone()
+        out = w(ids, x).cpu().numpy()
+        assert torch.equal(x, x0)  # the reference returns a new tensor when it changes scores
+        assert G.lookback_close(out, c["out"][t], 16) == [], t
+    w.reset()  # forgets the previous scores: the next call is a first call again
+    ids = torch.from_numpy(c["input_ids"][:, : m["prefix"] + 1]).to(cuda_device)
+    out = w(ids, torch.from_numpy(c["scores"][0]).to(cuda_device)).cpu().numpy()
+    assert G.lookback_close(out, c["out"][0], 16) == []
+
+
+@pytest.mark.gpu
+def test_build_logits_processor_list_with_lookback_matches_reference(cuda_device):
+    c = G.case("lookback_chain")
+    m = c["meta"]
+    procs = LP.build_logits_processor_list(G.lookback_tokenizer(m), cfg_scale=m["cfg"], timeshift_bias=m["bias"],
+                                           types_first=True, temperature=m["temps"][0],
+                                           timing_temperature=m["temps"][1], lookback_time=m["lookback_time"])
+    for t in range(m["steps"]):
+        ids = torch.from_numpy(c["input_ids"][:, : m["prefix"] + t + 1]).to(cuda_device)
+        out = procs(ids, torch.from_numpy(c["logits"][t]).to(cuda_device)).cpu().numpy()
+        assert G.lookback_close(out, c["processed"][t], 16) == [], t
+
+
+@pytest.mark.gpu
+def test_fused_sampler_with_lookback_matches_oracle(cuda_device):
+    from tests.harness import workloads as W
+    from oracle import oracle
+
+    s0 = W.lookback_decode(seed=21, pairs=48, vocab=4096, dtype="bf16")
+    timed = [t for t in range(4096) if (s0.lb_timed_bits[t >> 5] >> (t & 31)) & 1]
+    spec = {"mode": N.LOOKBACK_RENORM, "start": s0.lb_start, "end": s0.lb_end, "eos_ids": s0.lb_eos_ids,
+            "timed": timed}
+    fs = S.FusedSampler(vocab_size=4096, num_rows=48, device=cuda_device, cfg_scale=1.5, temperature=0.9, top_k=40,
+                        top_p=0.9, lookback=spec, return_logprobs=True)
+    state = np.full(48, np.nan, dtype=np.float32)
+    with pytest.raises(ValueError):
+        fs.step(torch.zeros((96, 4096), device=cuda_device))  # the bias needs input_ids
+    for step in range(4):
+        host = W.lookback_decode(seed=21, pairs=48, vocab=4096, dtype="bf16", step=step, lb_state=state)
+        host = host.with_(mono_mode=N.MONO_OFF, mono_state=None, want_logprobs=True)
+        ref = oracle.run(host)
+        logits = torch.from_numpy(W.bf16_to_f32(host.logits)).to(cuda_device).to(torch.bfloat16)
+        ids = fs.step(logits, torch.from_numpy(host.input_ids).to(cuda_device),
+                      uniforms=torch.from_numpy(host.uniforms).to(cuda_device))
+        torch.cuda.synchronize()
+        assert np.array_equal(ids.cpu().numpy(), ref["out_ids"]), step
+        got_state = fs.lb_state.cpu().numpy()
+        assert np.array_equal(got_state.view(np.uint32), ref["lb_state"].view(np.uint32)) or \
+            np.array_equal(got_state, ref["lb_state"], equal_nan=True)
+        state = ref["lb_state"]
+    fs.reset()
+    assert torch.isnan(fs.lb_state).all()

@@ -32,11 +32,11 @@ def forced(s):
     if _kernel["name"] == "warp" and s.vocab > 4096:
         pytest.skip("row-per-warp kernel: vocab <= 4096")
     s = s.with_(flags=(s.flags & ~_ALL_KERNEL_FLAGS) | _KERNEL_FLAGS[_kernel["name"]])
-    if _kernel["name"] == "stream":
+    if _kernel["name"] != "cta":
         arrays = host_arrays(s)
         args = fill_args(N.new_args(), s, lambda k: arrays[k].ctypes.data if k in arrays else 0)
         if N.validate(args) == N.ERR_UNSUPPORTED:
-            pytest.skip("streaming kernel does not serve this request")
+            pytest.skip(f"{_kernel['name']} kernel does not serve this request")
     return s
 
 
@@ -413,3 +413,49 @@ def test_row_warp_copy_timeout_marks_every_remaining_row(cuda_device):
     assert (got["out_status"] & N.ROW_COPY_TIMEOUT).all()
     assert (got["out_ids"] == 11).all()
     assert_parity(s, cuda_device)  # the same rows again, without the hook
+
+
+# ---------------------------------------------------------------- lookback bias
+@pytest.mark.parametrize("name", G.LOOKBACK_CASES)
+def test_lookback_fixture_steps(cuda_device, name):
+    # the reference fixtures' consecutive calls: kernel == oracle bit for bit
+    # (scores and lb_state), the kernel's state carried to the next call
+    c = G.case(name)
+    B = c["input_ids"].shape[0]
+    state = np.full(B, np.nan, dtype=np.float32)
+    for t in range(c["meta"]["steps"]):
+        ref, got = assert_parity(G.lookback_step(name, t, state), cuda_device)
+        assert G.lookback_close(got["out_scores"], G.lookback_reference(name, t), 16) == [], t
+        if "lb_state" in got:
+            state = got["lb_state"]
+
+
+@pytest.mark.parametrize("vocab,pairs,dtype", [(4096, 64, "bf16"), (4096, 512, "f32"), (32768, 4, "bf16"),
+                                               (131072, 2, "f16")])
+def test_lookback_sampling_steps(cuda_device, vocab, pairs, dtype):
+    # CFG + monotonic + temperature + lookback + top-k + top-p + draw over four
+    # steps; clusters for the large vocabularies
+    state = None
+    for step in range(4):
+        s = W.lookback_decode(seed=vocab + pairs, pairs=pairs, vocab=vocab, dtype=dtype, step=step, lb_state=state)
+        s = s.with_(want_scores=step % 2 == 0, want_logprobs=step % 2 == 1)
+        ref, got = assert_parity(s, cuda_device)
+        state = got["lb_state"]
+        assert np.isfinite(state).mean() > 0.9
+
+
+def test_lookback_edges(cuda_device):
+    # empty range (lb_start == lb_end), p = 1 (NaN at lb_start), p = 0, a NaN row,
+    # an all -inf row, an empty history, and the mask form
+    s = W.lookback_decode(seed=3, pairs=8, vocab=1000, dtype="f32")
+    x = s.logits.copy()
+    x[4] = np.nan
+    x[12] = -np.inf
+    x[5] = -np.inf
+    state = np.array([1.0, 0.0, 0.5, np.nan, 0.3, 0.3, 0.99999994, 1e-30], dtype=np.float32)
+    s = s.with_(logits=x, lb_state=state, want_scores=True, want_logprobs=True)
+    assert_parity(s, cuda_device)
+    assert_parity(s.with_(lb_end=s.lb_start), cuda_device)
+    assert_parity(s.with_(input_ids=s.input_ids[:, :0]), cuda_device)
+    assert_parity(s.with_(lookback_mode=N.LOOKBACK_MASK), cuda_device)
+    assert_parity(s.with_(lookback_mode=N.LOOKBACK_MASK, lb_end=1000, lb_start=990), cuda_device)

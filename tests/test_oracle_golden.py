@@ -164,3 +164,100 @@ def test_oracle_decode_loop_pad_and_finished(name):
         assert np.array_equal(r["out_ids"], want[:, t]), t
         unf = r["unfinished"]
     assert not unf.any()
+
+
+def test_lookback_spec_from_tokenizer():
+    # logit_processors.py:127-141 on the fixture's layout: TIME_SHIFT values from -20,
+    # lookback 300 ms -> value 30 -> ids [16, 16 + 20 + 30); eos + context eos; timed ids
+    from mapperatorinator_b200.logit_processors import lookback_spec
+
+    m = G.case("lookback_renorm")["meta"]
+    tok = G.lookback_tokenizer(m)
+    spec = lookback_spec(m["lookback_time"], tok, True)
+    assert (spec["start"], spec["end"]) == (16, 66)
+    assert spec["eos_ids"] == (2, 4, 5)
+    assert spec["mode"] == N.LOOKBACK_RENORM
+    assert sorted(spec["timed"]) == sorted(t for k, (a, b) in m["extra"].items() if k != "SCROLL_SPEED"
+                                           for t in range(a, b))
+    assert lookback_spec(m["lookback_time"], tok, False)["mode"] == N.LOOKBACK_MASK
+    with pytest.raises(ValueError):
+        lookback_spec(2000.0, tok, True)  # value 200 > max 79
+
+
+@pytest.mark.parametrize("name", G.LOOKBACK_CASES)
+def test_lookback_oracle_matches_reference(name):
+    # consecutive calls carry the previous EOS probability; step 0 has none (no bias)
+    c = G.case(name)
+    steps, B = c["meta"]["steps"], c["input_ids"].shape[0]
+    state = np.full(B, np.nan, dtype=np.float32)
+    transformed = 0
+    for t in range(steps):
+        r = oracle.run(G.lookback_step(name, t, state))
+        ref = G.lookback_reference(name, t)
+        assert G.lookback_close(r["out_scores"], ref, 16) == [], t
+        if c["meta"]["types_first"]:
+            state = r["lb_state"]
+            assert np.isfinite(state).all()
+            transformed += int(np.isneginf(ref[:, 17:66]).all(axis=1).sum())
+    if c["meta"]["types_first"]:
+        assert transformed >= 8  # the fixture exercises the bias on many rows
+
+
+def test_lookback_state_nan_rows_and_edge_values():
+    # a row with NaN stores NaN and is left alone; p = 1 gives a NaN lb_start score (reference: 0/0)
+    from mapperatorinator_b200.logit_processors import lookback_spec
+
+    m = G.case("lookback_renorm")["meta"]
+    spec = lookback_spec(m["lookback_time"], G.lookback_tokenizer(m), True)
+    rng = np.random.default_rng(5)
+    x = rng.normal(size=(3, 256)).astype(np.float32)
+    x[1, 7] = np.nan
+    ids = np.full((3, 2), 140, dtype=np.int64)
+    s = G.StepInputs(logits=x, dtype="f32", num_rows=3, input_ids=ids, select_mode=N.SELECT_NONE, want_scores=True,
+                     lookback_mode=N.LOOKBACK_RENORM, lb_start=spec["start"], lb_end=spec["end"],
+                     lb_eos_ids=spec["eos_ids"], lb_timed_bits=G.bits_for(spec["timed"], 256),
+                     lb_state=np.array([0.25, 0.25, 1.0], dtype=np.float32))
+    r = oracle.run(s)
+    assert np.isnan(r["lb_state"][1]) and np.isfinite(r["lb_state"][[0, 2]]).all()
+    out = r["out_scores"]
+    assert np.array_equal(out[1], x[1], equal_nan=True)
+    assert np.isfinite(out[0, spec["start"]]) and np.isneginf(out[0, spec["start"] + 1: spec["end"]]).all()
+    assert np.isnan(out[2, spec["start"]])
+
+
+def test_log_d_accuracy():
+    import math
+
+    rng = np.random.default_rng(0)
+    xs = np.concatenate([rng.uniform(0, 4, 2000), np.exp(rng.uniform(-700, 700, 2000)), [1.0, 0.5, 2.0, 5e-324]])
+    for x in xs:
+        got, want = oracle.log_d(float(x)), math.log(float(x))
+        assert abs(got - want) <= 4e-16 * max(abs(want), 1e-300) + (0.0 if want else 0.0), x
+    assert oracle.log_d(0.0) == -math.inf and math.isnan(oracle.log_d(-1.0))
+
+
+@pytest.mark.parametrize("name", ["lookback_renorm", "lookback_chain"])
+def test_lookback_extra_mass_against_float64(name):
+    # the EOS mass moved to lb_start, evaluated in float64 from the unbiased
+    # scores (bit-exact to the reference chain): within 2e-8 of it
+    c = G.case(name)
+    B = c["input_ids"].shape[0]
+    state, prev = np.full(B, np.nan, dtype=np.float32), None
+    checked = 0
+    for t in range(c["meta"]["steps"]):
+        s = G.lookback_step(name, t, state)
+        pre = oracle.run(s.with_(lookback_mode=N.LOOKBACK_OFF))["out_scores"].astype(np.float64)
+        r = oracle.run(s)
+        P = np.exp(pre - pre.max(axis=1, keepdims=True))
+        P /= P.sum(axis=1, keepdims=True)
+        if prev is not None:
+            p = prev[:, [2, 4, 5]].sum(axis=1)
+            O = P[:, np.r_[0:16, 66:256]].sum(axis=1)
+            sv = 1.0 / (O * (1.0 - p) + p)
+            extra = np.clip((sv - 1.0) * p / (1.0 - p), 0.0, 1.0)
+            on = np.isneginf(r["out_scores"][:, 17:66]).all(axis=1)
+            got = np.exp(r["out_scores"][on, 16].astype(np.float64))
+            assert np.abs(got - extra[on]).max(initial=0.0) <= 2e-8, t
+            checked += int(on.sum())
+        prev, state = P, r["lb_state"]
+    assert checked >= 8
