@@ -77,6 +77,8 @@ typedef enum MtrStatus {
 #define MTR_ROW_TIE_AT_CUT  (1u << 5) /* the top-p cut split equal scores (info)  */
 #define MTR_ROW_COPY_TIMEOUT (1u << 6) /* a staged row copy never landed: this row and every later row of
                                           the same CTA get pad_id and this bit (row-per-warp kernel) */
+#define MTR_ROW_APPEND_SKIPPED (1u << 7) /* the id-buffer column (*cur_len_dev) was outside [0, row stride):
+                                           the token was not appended */
 
 typedef enum MtrDType { MTR_DTYPE_F32 = 0, MTR_DTYPE_BF16 = 1, MTR_DTYPE_F16 = 2 } MtrDType;
 typedef enum MtrIdType { MTR_IDS_I64 = 0, MTR_IDS_I32 = 1 } MtrIdType;
@@ -231,6 +233,23 @@ typedef struct MtrSamplerArgs {
   int32_t lb_eos_ids[MTR_MAX_LB_EOS];  /* eos and context-eos ids (a repeated id counts twice) */
   const uint32_t* lb_timed_bits;   /* [ceil(V/32)] membership bitmap of timed-event ids */
   float* lb_state;                 /* [B] previous step's EOS probability, NaN = no previous step; rewritten */
+
+  /* ---- token append and stopping (optimized/single/decode_loop.py:303-316,
+   *      compiled_decode.py:1072-1080): with a selection, the emitted token
+   *      (pad_id for finished rows) is also written to id_buffer[row, cur],
+   *      cur = *cur_len_dev when given (a device value a CUDA graph can
+   *      advance between replays), else cur_len.  stop_counts accumulates over
+   *      launches (the caller zeroes it when a window starts):
+   *        [0] += rows still unfinished before this step whose token is an EOS
+   *               id (the compiled loop stops once it grows),
+   *        [1] += rows that finished in this step (needs unfinished; the HF
+   *               loop stops when it reaches B). ---- */
+  int64_t* id_buffer;              /* [B, id_buffer_row_stride] int64 or NULL */
+  int64_t id_buffer_row_stride;
+  const int32_t* cur_len_dev;      /* device column index or NULL */
+  int32_t cur_len;                 /* column index when cur_len_dev is NULL */
+  int32_t reserved1;
+  uint32_t* stop_counts;           /* [2] or NULL */
 } MtrSamplerArgs;
 
 /* Launch geometry chosen for a problem size (diagnostics and tests). */

@@ -45,6 +45,7 @@ ROW_BAD_UNIFORM = 1 << 3
 ROW_SLOW_PATH = 1 << 4
 ROW_TIE_AT_CUT = 1 << 5
 ROW_COPY_TIMEOUT = 1 << 6
+ROW_APPEND_SKIPPED = 1 << 7
 
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = 0, 1, 2
 IDS_I64, IDS_I32 = 0, 1
@@ -133,6 +134,12 @@ class MtrSamplerArgs(ctypes.Structure):
         ("lb_eos_ids", c_int32 * MAX_LB_EOS),
         ("lb_timed_bits", c_void_p),
         ("lb_state", c_void_p),
+        ("id_buffer", c_void_p),
+        ("id_buffer_row_stride", c_int64),
+        ("cur_len_dev", c_void_p),
+        ("cur_len", c_int32),
+        ("reserved1", c_int32),
+        ("stop_counts", c_void_p),
     ]
 
 

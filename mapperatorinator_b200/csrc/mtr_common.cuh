@@ -367,6 +367,30 @@ __device__ __forceinline__ bool is_eos(const MtrSamplerArgs& a, int64_t t) {
   return e;
 }
 
+// The end of a row's step, shared by every kernel (decode_loop.py:303-316):
+// finished rows emit pad_id, EOS clears unfinished, the token is appended to
+// the id buffer and the stop counters move.  Returns the emitted token; sets
+// MTR_ROW_APPEND_SKIPPED in *status for an out-of-range id-buffer column.
+__device__ __forceinline__ int64_t finish_token(const MtrSamplerArgs& a, int64_t row, int64_t tok, uint32_t* status) {
+  bool live = true;
+  if (a.unfinished) {
+    live = a.unfinished[row] != 0;
+    if (!live) tok = a.pad_id;
+  }
+  const bool eos = is_eos(a, tok);
+  if (a.unfinished) a.unfinished[row] = (uint8_t)(live && !eos);
+  if (a.stop_counts && live && eos) {
+    atomicAdd(a.stop_counts, 1u);
+    if (a.unfinished) atomicAdd(a.stop_counts + 1, 1u);
+  }
+  if (a.id_buffer) {
+    const int32_t cur = a.cur_len_dev ? *a.cur_len_dev : a.cur_len;
+    if (cur >= 0 && (int64_t)cur < a.id_buffer_row_stride) a.id_buffer[row * a.id_buffer_row_stride + cur] = tok;
+    else *status |= MTR_ROW_APPEND_SKIPPED;
+  }
+  return tok;
+}
+
 // bits [lo, hi) of an 8-bit chunk mask (empty when hi <= lo)
 __device__ __forceinline__ uint32_t range_bits(int lo, int hi) {
   lo = max(lo, 0);

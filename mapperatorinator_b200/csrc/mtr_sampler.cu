@@ -1666,12 +1666,7 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
   if (crank == owner && tid == 0) {
     int32_t m = sm.mono;
     if (sel != MTR_SELECT_NONE) {
-      int64_t fin = token;
-      if (a.unfinished) {
-        const uint8_t uf = a.unfinished[row];
-        if (!uf) fin = a.pad_id;
-        a.unfinished[row] = (uint8_t)(uf && !is_eos(a, fin));
-      }
+      const int64_t fin = finish_token(a, row, token, &gstatus);
       if (a.flags & MTR_FLAG_MONO_UPDATE_FROM_SAMPLE) m = mono_update(a, m, fin);
       if ((a.flags & MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE) && a.prev_token) a.prev_token[row] = (int32_t)fin;
       if (a.out_ids) a.out_ids[row] = fin;
@@ -2349,6 +2344,10 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
         for (int64_t r = row + (int64_t)lane * gridDim.x; r < a.num_rows; r += (int64_t)32 * gridDim.x) {
           if (a.out_status) a.out_status[r] = (r == row ? status : 0u) | MTR_ROW_COPY_TIMEOUT;
           if (sel != MTR_SELECT_NONE && a.out_ids) a.out_ids[r] = a.pad_id;
+          if (sel != MTR_SELECT_NONE && a.id_buffer) {
+            const int32_t cur = a.cur_len_dev ? *a.cur_len_dev : a.cur_len;
+            if (cur >= 0 && (int64_t)cur < a.id_buffer_row_stride) a.id_buffer[r * a.id_buffer_row_stride + cur] = a.pad_id;
+          }
         }
         mbar_wait(&mbar, parity ^ 1u);  // bounded: a late copy still owns X
         return;
@@ -3269,12 +3268,7 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
     if (lane == 0) {
       int32_t mm = mono;
       if (sel != MTR_SELECT_NONE) {
-        int64_t fin = token;
-        if (a.unfinished) {
-          const uint8_t uf = a.unfinished[row];
-          if (!uf) fin = a.pad_id;
-          a.unfinished[row] = (uint8_t)(uf && !is_eos(a, fin));
-        }
+        const int64_t fin = finish_token(a, row, token, &status);
         if (a.flags & MTR_FLAG_MONO_UPDATE_FROM_SAMPLE) mm = mono_update(a, mm, fin);
         if ((a.flags & MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE) && a.prev_token) a.prev_token[row] = (int32_t)fin;
         if (a.out_ids) a.out_ids[row] = fin;
@@ -3437,6 +3431,14 @@ static int validate(const MtrSamplerArgs* a) {
   if (a->lookback_mode != MTR_LOOKBACK_OFF) {
     if (a->flags & (MTR_FLAG_KERNEL_ROW_WARP | MTR_FLAG_KERNEL_STREAM)) return MTR_ERR_UNSUPPORTED;
     if (a->lb_start < 0 || a->lb_end < a->lb_start || a->lb_end > a->vocab) return MTR_ERR_BAD_SHAPE;
+  }
+  // token append and stop counters
+  if ((a->id_buffer || a->stop_counts) && a->select_mode == MTR_SELECT_NONE) return MTR_ERR_BAD_PARAM;
+  if ((uintptr_t)a->stop_counts % 4) return MTR_ERR_ALIGNMENT;
+  if (a->id_buffer) {
+    if ((uintptr_t)a->id_buffer % 8 || (uintptr_t)a->cur_len_dev % 4) return MTR_ERR_ALIGNMENT;
+    if (a->id_buffer_row_stride < 1) return MTR_ERR_BAD_SHAPE;
+    if (!a->cur_len_dev && (a->cur_len < 0 || a->cur_len >= a->id_buffer_row_stride)) return MTR_ERR_BAD_SHAPE;
   }
   if (a->lookback_mode == MTR_LOOKBACK_RENORM) {
     if (a->lb_start >= a->vocab) return MTR_ERR_BAD_SHAPE;

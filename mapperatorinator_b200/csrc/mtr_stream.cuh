@@ -1460,13 +1460,10 @@ __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constan
     // ---------------- epilogue
     st = g.or_u32(st);
     if (gt == 0) {
-      const uint32_t status = st | h.status;
+      uint32_t status = st | h.status;
       if (a.select_mode != MTR_SELECT_NONE) {
-        int64_t tok = (select_row && s.token >= 0) ? (int64_t)s.token : a.pad_id;
-        if (a.unfinished) {
-          if (!a.unfinished[row]) tok = a.pad_id;
-          a.unfinished[row] = (uint8_t)(a.unfinished[row] && !is_eos(a, tok));
-        }
+        const int64_t tok =
+            finish_token(a, row, (select_row && s.token >= 0) ? (int64_t)s.token : a.pad_id, &status);
         if (a.flags & MTR_FLAG_MONO_UPDATE_FROM_SAMPLE) mono = mono_update(a, mono, tok);
         if ((a.flags & MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE) && a.prev_token) a.prev_token[row] = (int32_t)tok;
         if (a.out_ids) a.out_ids[row] = tok;

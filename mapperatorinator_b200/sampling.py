@@ -257,6 +257,8 @@ class FusedSampler:
         self.unfinished = torch.ones(B, dtype=torch.uint8, device=self.device)
         if track_finished:
             a.unfinished = self.unfinished.data_ptr()
+        # cumulative since reset(): [0] live rows that emitted an EOS id, [1] rows finished
+        self.stop_counts = torch.zeros(2, dtype=torch.int32, device=self.device)
         a.pad_id = int(pad_token_id)
         if len(eos_token_ids) > N.MAX_EOS_IDS or len(eos_ranges) > N.MAX_EOS_RANGES:
             raise ValueError("too many eos ids / ranges")
@@ -292,11 +294,12 @@ class FusedSampler:
         self.mono_state.fill_(-1)
         self.prev_token.fill_(-1)
         self.unfinished.fill_(1)
+        self.stop_counts.zero_()
         self.lb_state.fill_(float("nan"))
         self._scan_next = self._base.mono_mode != N.MONO_OFF
         self._prev_from_ids_next = self.grammar is not None
 
-    def _args(self, logits: torch.Tensor, input_ids, uniforms) -> N.MtrSamplerArgs:
+    def _args(self, logits: torch.Tensor, input_ids, uniforms, id_buffer=None, cur_len=None) -> N.MtrSamplerArgs:
         a = N.MtrSamplerArgs()
         ctypes.pointer(a)[0] = self._base
         set_logits(a, logits)
@@ -316,6 +319,24 @@ class FusedSampler:
             a.flags |= N.FLAG_GRAMMAR_PREV_FROM_IDS
         if a.select_mode == N.SELECT_SAMPLE:
             a.uniforms = uniforms.data_ptr()
+        if a.select_mode != N.SELECT_NONE:
+            a.stop_counts = self.stop_counts.data_ptr()
+        if id_buffer is not None:
+            _require_cuda(id_buffer, "id_buffer")
+            if id_buffer.dtype != torch.int64 or id_buffer.dim() != 2 or id_buffer.shape[0] != self.num_rows \
+                    or id_buffer.stride(1) != 1:
+                raise ValueError("id_buffer must be an int64 [num_rows, S] tensor with unit column stride")
+            a.id_buffer = id_buffer.data_ptr()
+            a.id_buffer_row_stride = id_buffer.stride(0)
+            if isinstance(cur_len, torch.Tensor):
+                _require_cuda(cur_len, "cur_len")
+                if cur_len.dtype != torch.int32 or cur_len.numel() != 1:
+                    raise ValueError("a device cur_len must be a one-element int32 tensor")
+                a.cur_len_dev = cur_len.data_ptr()
+            else:
+                if cur_len is None or not 0 <= int(cur_len) < id_buffer.shape[1]:
+                    raise ValueError(f"cur_len {cur_len} outside the id buffer's {id_buffer.shape[1]} columns")
+                a.cur_len = int(cur_len)
         return a
 
     def launch_info(self, logits: torch.Tensor, input_ids: torch.Tensor | None = None,
@@ -327,17 +348,33 @@ class FusedSampler:
         return N.query_args(self._args(logits, input_ids, uniforms))
 
     def step(self, logits: torch.Tensor, input_ids: torch.Tensor | None = None,
-             uniforms: torch.Tensor | None = None, generator: torch.Generator | None = None) -> torch.Tensor:
+             uniforms: torch.Tensor | None = None, generator: torch.Generator | None = None, *,
+             id_buffer: torch.Tensor | None = None, cur_len=None) -> torch.Tensor:
         """Process one decoder step's logits ([B, V], or [2B, V] with CFG) and
         return the next tokens ``LongTensor[B]`` (a view of an internal buffer
-        that the next step overwrites)."""
+        that the next step overwrites).
+
+        With ``id_buffer`` (int64 [B, S]) the emitted tokens are also written to
+        column ``cur_len`` -- an int, or a one-element int32 CUDA tensor that a
+        captured graph advances between replays (compiled_decode.py:1072's
+        ``id_buffer[:, cur_len] = next_token``).  ``stop_counts`` then tells the
+        loop when to stop without a per-step host sync."""
         _require_cuda(logits, "logits")
         if self._base.select_mode == N.SELECT_SAMPLE:
             uniforms = _uniforms(self.num_rows, logits.device, uniforms, generator)
-        a = self._args(logits, input_ids, uniforms)
+        a = self._args(logits, input_ids, uniforms, id_buffer, cur_len)
         N.launch(a, torch.cuda.current_stream(logits.device).cuda_stream)
         if input_ids is not None:
             self._scan_next = False
             self._prev_from_ids_next = False
         self._last_uniforms = uniforms  # keep alive until the kernel has consumed them
         return self.out_ids
+
+    def any_eos(self) -> bool:
+        """A live row has emitted an EOS id since reset() (compiled_decode.py:1078's
+        stop test; one host sync)."""
+        return bool(self.stop_counts[0].item() > 0)
+
+    def all_finished(self) -> bool:
+        """Every row has finished (the HF loop's stop test; needs track_finished; one host sync)."""
+        return bool(self.stop_counts[1].item() >= self.num_rows)

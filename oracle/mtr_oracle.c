@@ -31,7 +31,7 @@
  *                  types_first = False masks [lb_start, lb_end); True
  *                  renormalises away that range after a timed-event token
  *                  (lookback_renorm below)
- *   top-k         remove scores < k-th largest score (ties kept)
+ *   top-k          remove scores < k-th largest score (ties kept)
  *                  (logits_process.py:581-588)
  *   top-p          nucleus over probabilities, see below
  *                  (logits_process.py:521-535 and compiled_decode.py:1147-1155)
@@ -534,10 +534,25 @@ int mtr_oracle_run(const MtrSamplerArgs* a) {
       }
     }
     if (a->select_mode != MTR_SELECT_NONE) {
+      /* pad, EOS, append, stop counters (decode_loop.py:303-316, compiled_decode.py:1072-1080) */
       int64_t final_tok = token;
+      int live = 1;
       if (a->unfinished) {
-        if (!a->unfinished[r]) final_tok = a->pad_id;
-        a->unfinished[r] = (uint8_t)(a->unfinished[r] && !is_eos(a, final_tok));
+        live = a->unfinished[r] != 0;
+        if (!live) final_tok = a->pad_id;
+      }
+      int eos = is_eos(a, final_tok);
+      if (a->unfinished) a->unfinished[r] = (uint8_t)(live && !eos);
+      if (a->stop_counts && live && eos) {
+        a->stop_counts[0] += 1u;
+        if (a->unfinished) a->stop_counts[1] += 1u;
+      }
+      if (a->id_buffer) {
+        int32_t cur = a->cur_len_dev ? *a->cur_len_dev : a->cur_len;
+        if (cur >= 0 && (int64_t)cur < a->id_buffer_row_stride)
+          a->id_buffer[r * a->id_buffer_row_stride + cur] = final_tok;
+        else
+          status |= MTR_ROW_APPEND_SKIPPED;
       }
       if (a->flags & MTR_FLAG_MONO_UPDATE_FROM_SAMPLE) mono = mono_update(a, mono, final_tok);
       if ((a->flags & MTR_FLAG_GRAMMAR_UPDATE_FROM_SAMPLE) && a->prev_token)

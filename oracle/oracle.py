@@ -103,12 +103,15 @@ def compare(ref: dict, got: dict, *, lp_rtol: float = 1e-5, lp_atol: float = 1e-
         info = np.uint32(N.ROW_SLOW_PATH)
         ref["out_status"] = ref["out_status"] & ~info
         got["out_status"] = got["out_status"] & ~info
-    for k in ("out_ids", "out_status", "mono_state", "prev_token", "unfinished"):
+    for k in ("out_ids", "out_status", "mono_state", "prev_token", "unfinished", "stop_counts"):
         if k in ref:
             if not np.array_equal(ref[k], got[k]):
                 bad = np.nonzero(ref[k] != got[k])[0]
                 errs.append(f"{k}: {len(bad)} rows differ, first {bad[:5].tolist()} "
                             f"ref {ref[k][bad[:5]].tolist()} got {got[k][bad[:5]].tolist()}")
+    if "id_buffer" in ref and not np.array_equal(ref["id_buffer"], got["id_buffer"]):
+        bad = np.argwhere(ref["id_buffer"] != got["id_buffer"])
+        errs.append(f"id_buffer: {len(bad)} entries differ, first {bad[:5].tolist()}")
     if "lb_state" in ref:
         r, g = ref["lb_state"], got["lb_state"]
         same = (r.view(np.uint32) == g.view(np.uint32)) | (np.isnan(r) & np.isnan(g))

@@ -103,6 +103,12 @@ def fill_args(args: N.MtrSamplerArgs, s: StepInputs, addr: Callable[[str], int],
         args.lb_eos_ids[i] = int(t)
     args.lb_timed_bits = addr("lb_timed_bits")
     args.lb_state = addr("lb_state")
+    if s.id_buffer is not None:
+        args.id_buffer = addr("id_buffer")
+        args.id_buffer_row_stride = int(s.id_buffer.shape[1])
+    args.cur_len = int(s.cur_len)
+    args.cur_len_dev = addr("cur_len_dev")
+    args.stop_counts = addr("stop_counts")
     return args
 
 
@@ -147,6 +153,12 @@ def host_arrays(s: StepInputs) -> dict:
         arr["lb_timed_bits"] = np.ascontiguousarray(s.lb_timed_bits, dtype=np.uint32)
     if s.lb_state is not None:
         arr["lb_state"] = np.array(s.lb_state, dtype=np.float32, copy=True)
+    if s.id_buffer is not None:
+        arr["id_buffer"] = np.array(s.id_buffer, dtype=np.int64, copy=True)
+    if s.cur_len_dev is not None:
+        arr["cur_len_dev"] = np.array(s.cur_len_dev, dtype=np.int32, copy=True).reshape(1)
+    if s.stop_counts is not None:
+        arr["stop_counts"] = np.array(s.stop_counts, dtype=np.uint32, copy=True).reshape(2)
     arr["out_ids"] = np.full(B, -7, dtype=np.int64)
     arr["out_status"] = np.full(B, 0xFFFFFFFF, dtype=np.uint32)
     if s.want_scores:
@@ -157,7 +169,7 @@ def host_arrays(s: StepInputs) -> dict:
 
 
 STATE_KEYS = ("out_ids", "out_status", "out_scores", "out_logprobs", "mono_state", "prev_token", "unfinished",
-              "lb_state")
+              "lb_state", "id_buffer", "stop_counts")
 
 
 class DeviceStep:
@@ -197,7 +209,7 @@ class DeviceStep:
             if t is None:
                 continue
             a = t.cpu().numpy()
-            if k == "out_status":
+            if k in ("out_status", "stop_counts"):
                 a = a.view(np.uint32)
             out[k] = a
         return out

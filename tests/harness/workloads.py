@@ -96,6 +96,11 @@ class StepInputs:
     lb_eos_ids: tuple = ()
     lb_timed_bits: np.ndarray | None = None  # [ceil(V/32)] uint32
     lb_state: np.ndarray | None = None       # [B] float32, NaN = no previous step
+    # token append and stop counters
+    id_buffer: np.ndarray | None = None      # [B, S] int64
+    cur_len: int = 0
+    cur_len_dev: np.ndarray | None = None    # [1] int32 (device-side column index)
+    stop_counts: np.ndarray | None = None    # [2] uint32
 
     @property
     def vocab(self) -> int:

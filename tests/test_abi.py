@@ -270,3 +270,22 @@ def test_lookback_validation_and_kernel(lib):
     b.input_ids = 0
     b.lb_timed_bits = 0  # no history: no last token to look up
     assert N.validate(b) == N.OK
+
+
+def test_append_and_stop_validation(lib):
+    a = _valid_args()
+    a.id_buffer, a.id_buffer_row_stride, a.cur_len = 0x90000, 64, 10
+    a.stop_counts = 0xA0000
+    assert N.validate(a) == N.OK
+    for field, value, code in (("cur_len", 64, N.ERR_BAD_SHAPE), ("cur_len", -1, N.ERR_BAD_SHAPE),
+                               ("id_buffer_row_stride", 0, N.ERR_BAD_SHAPE), ("id_buffer", 0x90004, N.ERR_ALIGNMENT),
+                               ("stop_counts", 0xA0002, N.ERR_ALIGNMENT), ("cur_len_dev", 0xB0002, N.ERR_ALIGNMENT),
+                               ("select_mode", N.SELECT_NONE, N.ERR_BAD_PARAM)):
+        b = _valid_args()
+        b.id_buffer, b.id_buffer_row_stride, b.cur_len = 0x90000, 64, 10
+        b.stop_counts = 0xA0000
+        setattr(b, field, value)
+        assert N.validate(b) == code, (field, value)
+    b = _valid_args()
+    b.id_buffer, b.id_buffer_row_stride, b.cur_len, b.cur_len_dev = 0x90000, 64, 1000, 0xB0000
+    assert N.validate(b) == N.OK  # a device column is checked by the kernel (MTR_ROW_APPEND_SKIPPED)

@@ -385,3 +385,70 @@ def test_fused_sampler_with_lookback_matches_oracle(cuda_device):
         state = ref["lb_state"]
     fs.reset()
     assert torch.isnan(fs.lb_state).all()
+
+
+@pytest.mark.gpu
+def test_fused_sampler_graph_step_appends_and_stops(cuda_device):
+    """A whole token step in one CUDA graph: a stand-in decoder (embedding of the
+    previous token -> lm_head matmul) and FusedSampler.step appending at a
+    device-side cur_len that the graph advances; compared with eager steps."""
+    from mapperatorinator_b200.sampling import FusedSampler
+
+    B, V, d, steps = 16, 512, 64, 12
+    g = torch.Generator(device=cuda_device).manual_seed(3)
+    emb = torch.randn((V, d), device=cuda_device, generator=g)
+    head = torch.randn((V, d), device=cuda_device, generator=g) * 0.5
+
+    def make():
+        return FusedSampler(vocab_size=V, num_rows=B, device=cuda_device, top_p=0.9, eos_token_ids=(3,),
+                            pad_token_id=0, track_finished=True)
+
+    uniforms = torch.rand((steps, B), device=cuda_device, generator=g)
+    # eager
+    eager = make()
+    buf_e = torch.full((B, steps + 4), -1, dtype=torch.int64, device=cuda_device)
+    buf_e[:, :2] = 1
+    for t in range(steps):
+        logits = emb[buf_e[:, 1 + t]] @ head.T
+        eager.step(logits, buf_e[:, : 2 + t], uniforms=uniforms[t], id_buffer=buf_e, cur_len=2 + t)
+    # graph: one capture of the whole step, replayed `steps` times
+    fs = make()
+    buf = torch.full((B, steps + 4), -1, dtype=torch.int64, device=cuda_device)
+    buf[:, :2] = 1
+    cur = torch.tensor([2], dtype=torch.int32, device=cuda_device)
+    u = torch.empty(B, device=cuda_device)
+    prev = torch.empty(B, dtype=torch.int64, device=cuda_device)
+
+    def one_step():
+        prev.copy_(buf.gather(1, (cur.long() - 1).expand(B, 1)).squeeze(1))
+        logits = emb[prev] @ head.T
+        fs.step(logits, None, uniforms=u, id_buffer=buf, cur_len=cur)
+        cur.add_(1)
+
+    s = torch.cuda.Stream(cuda_device)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        u.copy_(uniforms[0])
+        one_step()  # warm-up outside the capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    buf[:, 2:] = -1
+    cur.fill_(2)
+    fs.reset()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        one_step()
+    torch.cuda.synchronize()
+    buf[:, 2:] = -1
+    cur.fill_(2)
+    fs.reset()
+    for t in range(steps):
+        u.copy_(uniforms[t])
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(buf, buf_e)
+    assert torch.equal(fs.stop_counts, eager.stop_counts)
+    assert torch.equal(fs.unfinished, eager.unfinished)
+    assert fs.all_finished() == eager.all_finished()
+    assert int(cur.item()) == 2 + steps
+    del graph

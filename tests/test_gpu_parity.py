@@ -459,3 +459,29 @@ def test_lookback_edges(cuda_device):
     assert_parity(s.with_(input_ids=s.input_ids[:, :0]), cuda_device)
     assert_parity(s.with_(lookback_mode=N.LOOKBACK_MASK), cuda_device)
     assert_parity(s.with_(lookback_mode=N.LOOKBACK_MASK, lb_end=1000, lb_start=990), cuda_device)
+
+
+# ---------------------------------------------------------------- token append and stop counters
+@pytest.mark.parametrize("workload", ["batched", "penalty"])
+def test_append_and_stop_counts(cuda_device, workload):
+    # pad-on-finished, EOS (ids and a range), id-buffer column from a host value
+    # and from a device value, cumulative stop counters -- on every kernel
+    if workload == "batched":
+        s = W.batched_decode(seed=63, pairs=48)
+        B = 48
+    else:
+        s = W.penalty_sweep(seed=64, rows=1024).with_(top_p=0.9)
+        B = 1024
+    rng = np.random.default_rng(65)
+    unf = (rng.random(B) < 0.8).astype(np.uint8)
+    buf = np.full((B, 40), -1, dtype=np.int64)
+    counts = np.array([3, 5], dtype=np.uint32)  # cumulative: earlier steps' counts stay
+    s = s.with_(unfinished=unf, pad_id=7, eos_ids=(5, 9), eos_ranges=((0, 2048),), id_buffer=buf, cur_len=17,
+                stop_counts=counts)
+    ref, got = assert_parity(s, cuda_device)
+    assert (got["id_buffer"][:, 17] == got["out_ids"]).all()
+    assert ref["stop_counts"][1] > 5  # some rows finished in this step
+    ref, got = assert_parity(s.with_(cur_len_dev=np.array([39], dtype=np.int32)), cuda_device)
+    assert (got["id_buffer"][:, 39] == got["out_ids"]).all() and (got["id_buffer"][:, 17] == -1).all()
+    ref, got = assert_parity(s.with_(cur_len_dev=np.array([40], dtype=np.int32)), cuda_device)
+    assert (got["out_status"] & N.ROW_APPEND_SKIPPED).all() and (got["id_buffer"] == -1).all()

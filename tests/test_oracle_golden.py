@@ -155,15 +155,39 @@ def test_oracle_decode_loop_pad_and_finished(name):
     sched, want = c["schedule"], c["generated"]
     steps, rows = sched.shape
     unf = np.ones(rows, dtype=np.uint8)
+    prompt = 3
+    buf = np.full((rows, prompt + steps + 2), -1, dtype=np.int64)
+    counts = np.zeros(2, dtype=np.uint32)
     for t in range(steps):
         x = np.full((rows, 8), -1000.0, dtype=np.float32)
         x[np.arange(rows), sched[t]] = 1000.0
         s = StepInputs(logits=x, dtype="f32", num_rows=rows, select_mode=N.SELECT_ARGMAX, unfinished=unf,
-                       pad_id=0, eos_ids=(2,))
+                       pad_id=0, eos_ids=(2,), id_buffer=buf, cur_len=prompt + t, stop_counts=counts)
         r = oracle.run(s)
         assert np.array_equal(r["out_ids"], want[:, t]), t
-        unf = r["unfinished"]
+        unf, buf, counts = r["unfinished"], r["id_buffer"], r["stop_counts"]
+        # the reference loop runs until every row has finished: [1] == rows exactly at its last step
+        assert (counts[1] == rows) == (t == steps - 1), t
+        assert counts[1] == rows - int(unf.sum())
     assert not unf.any()
+    # the appended columns are the reference loop's generated tokens (torch.cat at cur_len)
+    assert np.array_equal(buf[:, prompt: prompt + steps], want)
+    assert (buf[:, :prompt] == -1).all() and (buf[:, prompt + steps:] == -1).all()
+    # [0] counts live rows that emitted an EOS: one per row here
+    assert counts[0] == rows
+
+
+def test_oracle_append_skips_out_of_range_column():
+    from tests.harness.workloads import StepInputs
+
+    x = np.zeros((2, 8), dtype=np.float32)
+    buf = np.full((2, 4), -1, dtype=np.int64)
+    r = oracle.run(StepInputs(logits=x, dtype="f32", num_rows=2, select_mode=N.SELECT_ARGMAX, id_buffer=buf,
+                              cur_len_dev=np.array([4], dtype=np.int32)))
+    assert (r["out_status"] & N.ROW_APPEND_SKIPPED).all() and (r["id_buffer"] == -1).all()
+    r = oracle.run(StepInputs(logits=x, dtype="f32", num_rows=2, select_mode=N.SELECT_ARGMAX, id_buffer=buf,
+                              cur_len_dev=np.array([3], dtype=np.int32), cur_len=99))
+    assert (r["out_status"] == 0).all() and (r["id_buffer"][:, 3] == 0).all()
 
 
 def test_lookback_spec_from_tokenizer():
