@@ -265,6 +265,42 @@ typedef struct MtrLaunchInfo {
   int32_t kernel;         /* 0: row-per-CTA (cluster) kernel, 1: row-per-warp kernel, 2: streaming row-group kernel */
 } MtrLaunchInfo;
 
+/*
+ * The decoder's output projection on the tensor cores (tcgen05, TMA), writing
+ * the bf16 logits the sampler reads:
+ *   logits[r, v] = RN_bf16(sum_k hidden[r, k] * weight[v, k]), fp32 accumulation.
+ * Replaces VarWhisperForConditionalGeneration.proj_out (nn.Linear(d_model,
+ * vocab, bias=False) in bf16) at
+ * osuT5/osuT5/model/custom_transformers/modeling_varwhisper.py:1583, 1647-1649.
+ */
+typedef struct MtrLmHeadArgs {
+  uint32_t abi_version;         /* = MTR_ABI_VERSION */
+  uint32_t struct_size;         /* = sizeof(MtrLmHeadArgs) */
+  const void* hidden;           /* [rows, d_model] bf16, 16-byte aligned */
+  int64_t hidden_row_stride;    /* elements, multiple of 8 */
+  const void* weight;           /* [vocab, d_model] bf16 (nn.Linear weight), 16-byte aligned */
+  int64_t weight_row_stride;    /* elements, multiple of 8 */
+  void* logits;                 /* [rows, vocab] bf16 output, 16-byte aligned */
+  int64_t logits_row_stride;    /* elements, multiple of 8 */
+  int32_t rows;
+  int32_t d_model;              /* multiple of 64 */
+  int32_t vocab;                /* multiple of 8, <= MTR_MAX_VOCAB */
+  int32_t tile_n;               /* vocabulary ids per CTA: 0 = choose, 64 or 128 */
+  uint32_t* error_word;         /* device word or NULL: bits set when a bounded wait gave up */
+} MtrLmHeadArgs;
+
+/* Host-side checks of MtrLmHeadArgs (no CUDA call). */
+int mtr_lmhead_validate(const MtrLmHeadArgs* args);
+
+/* The projection alone, on `stream`. */
+int mtr_lmhead_launch(const MtrLmHeadArgs* args, void* stream);
+
+/* The projection, then mtr_sampler_launch on its logits as a programmatic
+ * dependent launch (the sampler's CTAs start while the projection drains and
+ * wait for its results).  sampler->logits must be lm->logits (bf16, same row
+ * stride and vocabulary) and the sampler's rows must lie inside lm->rows. */
+int mtr_lmhead_sample_launch(const MtrLmHeadArgs* lm, const MtrSamplerArgs* sampler, void* stream);
+
 /* ABI identity: MTR_ABI_VERSION and sizeof(MtrSamplerArgs) of the library. */
 int mtr_abi_version(void);
 size_t mtr_args_size(void);

@@ -162,6 +162,26 @@ KERNEL_ROW_WARP = 1
 KERNEL_STREAM = 2
 
 
+class MtrLmHeadArgs(ctypes.Structure):
+    """include/mtr_sampler.h MtrLmHeadArgs: the tensor-core output projection."""
+
+    _fields_ = [
+        ("abi_version", c_uint32),
+        ("struct_size", c_uint32),
+        ("hidden", c_void_p),
+        ("hidden_row_stride", c_int64),
+        ("weight", c_void_p),
+        ("weight_row_stride", c_int64),
+        ("logits", c_void_p),
+        ("logits_row_stride", c_int64),
+        ("rows", c_int32),
+        ("d_model", c_int32),
+        ("vocab", c_int32),
+        ("tile_n", c_int32),
+        ("error_word", c_void_p),
+    ]
+
+
 # Every symbol include/mtr_sampler.h declares: (name, restype, argtypes).
 EXPORTS = {
     "mtr_abi_version": (ctypes.c_int, []),
@@ -173,6 +193,10 @@ EXPORTS = {
     "mtr_sampler_launch": (ctypes.c_int, [ctypes.POINTER(MtrSamplerArgs), c_void_p]),
     "mtr_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "mtr_last_cuda_error": (ctypes.c_int, []),
+    "mtr_lmhead_validate": (ctypes.c_int, [ctypes.POINTER(MtrLmHeadArgs)]),
+    "mtr_lmhead_launch": (ctypes.c_int, [ctypes.POINTER(MtrLmHeadArgs), c_void_p]),
+    "mtr_lmhead_sample_launch": (ctypes.c_int, [ctypes.POINTER(MtrLmHeadArgs), ctypes.POINTER(MtrSamplerArgs),
+                                                c_void_p]),
 }
 
 
@@ -274,3 +298,24 @@ def query_args(args: MtrSamplerArgs) -> MtrLaunchInfo:
     info = MtrLaunchInfo()
     check(load().mtr_sampler_query_args(ctypes.byref(args), ctypes.byref(info)), "mtr_sampler_query_args")
     return info
+
+
+def new_lmhead_args() -> MtrLmHeadArgs:
+    a = MtrLmHeadArgs()
+    ctypes.memset(ctypes.byref(a), 0, ctypes.sizeof(a))
+    a.abi_version = ABI_VERSION
+    a.struct_size = ctypes.sizeof(a)
+    return a
+
+
+def lmhead_validate(args: MtrLmHeadArgs) -> int:
+    return load().mtr_lmhead_validate(ctypes.byref(args))
+
+
+def lmhead_launch(args: MtrLmHeadArgs, stream: int | None) -> None:
+    check(load().mtr_lmhead_launch(ctypes.byref(args), c_void_p(stream or 0)), "mtr_lmhead_launch")
+
+
+def lmhead_sample_launch(lm: MtrLmHeadArgs, args: MtrSamplerArgs, stream: int | None) -> None:
+    check(load().mtr_lmhead_sample_launch(ctypes.byref(lm), ctypes.byref(args), c_void_p(stream or 0)),
+          "mtr_lmhead_sample_launch")

@@ -20,7 +20,7 @@ CSRC = PKG_DIR / "csrc"
 LIB_DIR = PKG_DIR / "_lib"
 LIB_PATH = LIB_DIR / "libmtr_sampler.so"
 SOURCES = [CSRC / "mtr_sampler.cu", CSRC / "mtr_stream.cu", CSRC / "mtr_stream_bf16.cu", CSRC / "mtr_stream_f16.cu",
-           CSRC / "mtr_stream_f32.cu"]
+           CSRC / "mtr_stream_f32.cu", CSRC / "mtr_lmhead.cu"]
 HEADERS = [REPO_DIR / "include" / "mtr_sampler.h", CSRC / "mtr_common.cuh", CSRC / "mtr_stream.cuh"]
 BUILD_DIR = PKG_DIR / "_build"
 

@@ -452,6 +452,7 @@ struct Derived {
   // constant would let the compiler turn them into a mul + add pair and fuse it)
   float neg_one, neg_zero, one;
   float rep_rcp;  // RN(1 / repetition_penalty) when it lies in [2^-30, 2^30] (Markstein divide), else 0
+  int32_t pdl;    // launched as a programmatic dependent (host-side launch choice)
 };
 
 // Warp bitonic sort of 32*E distinct (or zero) u64 keys, descending; lane l
@@ -495,5 +496,35 @@ cudaError_t cached_occupancy(const void* kern, int threads, int dyn, int* occ);
 bool sk_supported(const MtrSamplerArgs& a, const Derived& d);
 cudaError_t stream_launch(const MtrSamplerArgs& a, const Derived& d, int sms, cudaStream_t s);
 void stream_query(const MtrSamplerArgs& a, const Derived& d, int sms, MtrLaunchInfo* out);
+
+// SM count of the current device (148 without a device), the thread's last CUDA
+// error, and the sampler launch (validated arguments); `pdl` launches it as a
+// programmatic dependent of the previous kernel on the stream (mtr_lmhead.cu).
+int device_sms();
+void set_last_cuda_error(int e);
+int sampler_launch(const MtrSamplerArgs* a, cudaStream_t s, bool pdl);
+
+// Launch attributes every sampler kernel launch shares: the cluster shape (when
+// CS > 1) and programmatic stream serialisation (when d.pdl).
+inline unsigned launch_attrs(cudaLaunchAttribute* at, int cs, bool pdl) {
+  unsigned n = 0;
+  if (cs > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = (unsigned)cs;
+    at[n].val.clusterDim.y = 1;
+    at[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  return n;
+}
+
+// Kernel entry: when launched as a programmatic dependent, wait for the
+// previous grid's results (a no-op otherwise).
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 }  // namespace mtr

@@ -275,6 +275,7 @@ __device__ __forceinline__ void collect(Shared<CS>& sm, uint32_t mask, const flo
 template <typename Tin, int THREADS, int EPT, int CS>
 __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     sampler_kernel(const __grid_constant__ MtrSamplerArgs a, const __grid_constant__ Derived dv) {
+  wait_prior_grid();
   using E = Elem<Tin>;
   constexpr int VEC = E::VEC;
   constexpr int NCH = EPT / VEC;
@@ -2035,6 +2036,7 @@ __device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derive
 template <typename Tin, bool CFG>
 __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant__ MtrSamplerArgs a,
                                                          const __grid_constant__ Derived dv) {
+  wait_prior_grid();
   using E = Elem<Tin>;
   constexpr int VEC = E::VEC;            // elements per 16-byte group
   constexpr int NV = 8 / VEC;            // 16-byte groups per 8-id chunk and side
@@ -3310,7 +3312,7 @@ static int dyn_smem_bytes(const Geo& g, bool pen) {
 
 // SM count of the current device (148 when no device is visible, e.g. for
 // geometry queries on a CPU-only host)
-static int device_sms() {
+int device_sms() {
   static int cache[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
@@ -3329,6 +3331,7 @@ static int device_sms() {
 }
 
 static thread_local int g_last_cuda_error = 0;
+void set_last_cuda_error(int e) { g_last_cuda_error = e; }
 
 static bool bad_float(float v) { return !(v == v) || v == INFINITY || v == -INFINITY; }
 
@@ -3505,15 +3508,9 @@ static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, 
   cfg.blockDim = dim3(TH, 1, 1);
   cfg.dynamicSmemBytes = (size_t)dyn;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  if (CS > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = CS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
+  cudaLaunchAttribute attr[2];
+  cfg.numAttrs = launch_attrs(attr, CS, d.pdl != 0);
+  cfg.attrs = cfg.numAttrs ? attr : nullptr;
   return cudaLaunchKernelEx(&cfg, kern, a, d);
 }
 
@@ -3608,6 +3605,9 @@ static cudaError_t launch_warp_t(const MtrSamplerArgs& a, const Derived& d, cuda
   cfg.blockDim = dim3(32, 1, 1);
   cfg.dynamicSmemBytes = (size_t)dyn;
   cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  cfg.numAttrs = launch_attrs(attr, 1, d.pdl != 0);
+  cfg.attrs = cfg.numAttrs ? attr : nullptr;
   return cudaLaunchKernelEx(&cfg, kern, a, d);
 }
 template <typename Tin>
@@ -3707,9 +3707,15 @@ int mtr_sampler_launch(const MtrSamplerArgs* a, void* stream) {
   const int v = mtr::validate_all(a);
   if (v != MTR_OK) return v;
   if (a->num_rows == 0) return MTR_OK;
-  const mtr::Derived d = mtr::derive(*a);
+  return mtr::sampler_launch(a, (cudaStream_t)stream, false);
+}
+
+}  // extern "C"
+
+int mtr::sampler_launch(const MtrSamplerArgs* a, cudaStream_t s, bool pdl) {
+  mtr::Derived d = mtr::derive(*a);
+  d.pdl = pdl ? 1 : 0;
   const int sms = mtr::device_sms();
-  cudaStream_t s = (cudaStream_t)stream;
   cudaError_t e;
   const int k = mtr::pick_kernel(*a, d, sms);
   if (k == mtr::KERNEL_STREAM) {
@@ -3732,6 +3738,8 @@ int mtr_sampler_launch(const MtrSamplerArgs* a, void* stream) {
   mtr::g_last_cuda_error = (int)e;
   return e == cudaSuccess ? MTR_OK : MTR_ERR_CUDA;
 }
+
+extern "C" {
 
 const char* mtr_status_string(int code) {
   switch (code) {

@@ -963,6 +963,7 @@ template <typename Tin, bool CFG, int MAXT, int MINB>
 __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constant__ MtrSamplerArgs a,
                                                           const __grid_constant__ Derived dv,
                                                           const __grid_constant__ SkGeo geo) {
+  wait_prior_grid();
   using T = SkT<Tin>;
   constexpr int NV = T::NV;
   const int tid = threadIdx.x;
@@ -1507,6 +1508,9 @@ cudaError_t stream_launch_f32(const MtrSamplerArgs& a, const Derived& d, const S
     cfg.blockDim = dim3((unsigned)sh.threads, 1, 1);                                                              \
     cfg.dynamicSmemBytes = (size_t)sh.dyn;                                                                        \
     cfg.stream = s;                                                                                               \
+    cudaLaunchAttribute attr[2];                                                                                  \
+    cfg.numAttrs = launch_attrs(attr, 1, d.pdl != 0);                                                             \
+    cfg.attrs = cfg.numAttrs ? attr : nullptr;                                                                    \
     const bool c = a.cfg_enabled != 0;                                                                            \
     if (sh.shape == SK_SHAPE_128)                                                                                 \
       return c ? cudaLaunchKernelEx(&cfg, stream_kernel<TIN, true, 128, 7>, a, d, g)                             \

@@ -82,6 +82,36 @@ def token_bitmap(tokens, vocab: int, device) -> torch.Tensor:
     return words.to(torch.int32).to(device)
 
 
+def _lmhead_args(hidden: torch.Tensor, weight: torch.Tensor, out: torch.Tensor, tile_n: int) -> N.MtrLmHeadArgs:
+    for t, what in ((hidden, "hidden"), (weight, "weight"), (out, "logits")):
+        _require_cuda(t, what)
+        if t.dtype != torch.bfloat16 or t.dim() != 2 or t.stride(1) != 1:
+            raise ValueError(f"{what} must be a 2-D bfloat16 CUDA tensor with unit column stride")
+    if hidden.shape[1] != weight.shape[1]:
+        raise ValueError(f"hidden d_model {hidden.shape[1]} != weight d_model {weight.shape[1]}")
+    if out.shape[0] != hidden.shape[0] or out.shape[1] != weight.shape[0]:
+        raise ValueError("logits must be [hidden rows, vocab]")
+    a = N.new_lmhead_args()
+    a.hidden, a.hidden_row_stride = hidden.data_ptr(), hidden.stride(0)
+    a.weight, a.weight_row_stride = weight.data_ptr(), weight.stride(0)
+    a.logits, a.logits_row_stride = out.data_ptr(), out.stride(0)
+    a.rows, a.d_model, a.vocab = hidden.shape[0], hidden.shape[1], weight.shape[0]
+    a.tile_n = int(tile_n)
+    return a
+
+
+def lm_head_logits(hidden: torch.Tensor, weight: torch.Tensor, out: torch.Tensor | None = None, *,
+                   tile_n: int = 0) -> torch.Tensor:
+    """``proj_out(hidden)`` (modeling_varwhisper.py:1583, an nn.Linear without
+    bias in bf16) on the tcgen05 tensor cores: bf16 ``[R, V]`` logits with fp32
+    accumulation.  ``hidden`` is ``[R, d]``, ``weight`` the Linear's ``[V, d]``."""
+    if out is None:
+        out = torch.empty((hidden.shape[0], weight.shape[0]), dtype=torch.bfloat16, device=hidden.device)
+    a = _lmhead_args(hidden, weight, out, tile_n)
+    N.lmhead_launch(a, torch.cuda.current_stream(hidden.device).cuda_stream)
+    return out
+
+
 def _uniforms(n: int, device, uniforms, generator) -> torch.Tensor:
     if uniforms is None:
         return torch.rand(n, device=device, generator=generator, dtype=torch.float32)
@@ -368,6 +398,35 @@ class FusedSampler:
             self._scan_next = False
             self._prev_from_ids_next = False
         self._last_uniforms = uniforms  # keep alive until the kernel has consumed them
+        return self.out_ids
+
+    def step_hidden(self, hidden: torch.Tensor, weight: torch.Tensor, input_ids: torch.Tensor | None = None,
+                    uniforms: torch.Tensor | None = None, generator: torch.Generator | None = None, *,
+                    id_buffer: torch.Tensor | None = None, cur_len=None, tile_n: int = 0) -> torch.Tensor:
+        """The decoder's last hidden states to the next tokens: the tensor-core
+        output projection (``lm_head_logits``) writes bf16 logits that this
+        step's fused kernel reads, launched as its programmatic dependent.
+        ``hidden`` has the logits' rows ([2B, d] with CFG).  The logits stay
+        readable in ``self.lm_logits`` until the next call."""
+        _require_cuda(hidden, "hidden")
+        rows = hidden.shape[0]
+        if rows != (2 * self.num_rows if self._base.cfg_enabled else self.num_rows):
+            raise ValueError(f"hidden has {rows} rows")
+        if weight.shape[0] != self.vocab_size:
+            raise ValueError(f"weight vocabulary {weight.shape[0]} != {self.vocab_size}")
+        buf = getattr(self, "lm_logits", None)
+        if buf is None or buf.shape != (rows, self.vocab_size) or buf.device != hidden.device:
+            buf = torch.empty((rows, self.vocab_size), dtype=torch.bfloat16, device=hidden.device)
+            self.lm_logits = buf
+        lm = _lmhead_args(hidden, weight, buf, tile_n)
+        if self._base.select_mode == N.SELECT_SAMPLE:
+            uniforms = _uniforms(self.num_rows, hidden.device, uniforms, generator)
+        a = self._args(buf, input_ids, uniforms, id_buffer, cur_len)
+        N.lmhead_sample_launch(lm, a, torch.cuda.current_stream(hidden.device).cuda_stream)
+        if input_ids is not None:
+            self._scan_next = False
+            self._prev_from_ids_next = False
+        self._last_uniforms = uniforms
         return self.out_ids
 
     def any_eos(self) -> bool:

@@ -289,3 +289,46 @@ def test_append_and_stop_validation(lib):
     b = _valid_args()
     b.id_buffer, b.id_buffer_row_stride, b.cur_len, b.cur_len_dev = 0x90000, 64, 1000, 0xB0000
     assert N.validate(b) == N.OK  # a device column is checked by the kernel (MTR_ROW_APPEND_SKIPPED)
+
+
+def _lm_args():
+    a = N.new_lmhead_args()
+    a.hidden, a.hidden_row_stride = 0x100000, 768
+    a.weight, a.weight_row_stride = 0x200000, 768
+    a.logits, a.logits_row_stride = 0x300000, 4096
+    a.rows, a.d_model, a.vocab = 256, 768, 4096
+    return a
+
+
+def test_lmhead_validation(lib):
+    assert N.lmhead_validate(_lm_args()) == N.OK  # also: the ctypes struct has the C size
+    for field, value, code in (("d_model", 100, N.ERR_BAD_SHAPE), ("d_model", 0, N.ERR_BAD_SHAPE),
+                               ("vocab", 4100, N.ERR_BAD_SHAPE), ("vocab", N.MAX_VOCAB + 8, N.ERR_BAD_SHAPE),
+                               ("rows", -1, N.ERR_BAD_SHAPE), ("tile_n", 32, N.ERR_BAD_PARAM),
+                               ("hidden", 0, N.ERR_NULL_ARG), ("weight", 0x200008, N.ERR_ALIGNMENT),
+                               ("logits_row_stride", 4095, N.ERR_BAD_SHAPE),
+                               ("hidden_row_stride", 772, N.ERR_ALIGNMENT), ("struct_size", 8, N.ERR_ABI)):
+        b = _lm_args()
+        setattr(b, field, value)
+        assert N.lmhead_validate(b) == code, field
+        # the launchers validate first: no CUDA call for bad input
+        assert lib.mtr_lmhead_launch(ctypes.byref(b), None) == code, field
+    b = _lm_args()
+    b.rows = 0
+    assert lib.mtr_lmhead_launch(ctypes.byref(b), None) == N.OK
+
+
+def test_lmhead_sample_pairing_checked(lib):
+    lm = _lm_args()
+    a = _valid_args()
+    a.logits, a.logits_row_stride, a.vocab, a.num_rows = lm.logits, 4096, 4096, 128
+    a.cfg_enabled, a.cfg_scale = 1, 1.5
+    # the sampler must read the projection's own buffer, as bf16, inside its rows
+    for field, value in (("logits", 0x400000), ("logits_dtype", N.DTYPE_F32), ("num_rows", 129)):
+        b = N.MtrSamplerArgs()
+        ctypes.pointer(b)[0] = a
+        setattr(b, field, value)
+        if field == "logits_dtype":
+            b.logits_row_stride = 4096
+        rc = lib.mtr_lmhead_sample_launch(ctypes.byref(lm), ctypes.byref(b), None)
+        assert rc in (N.ERR_BAD_PARAM, N.ERR_BAD_SHAPE), field
