@@ -60,7 +60,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--profile", type=int, default=0,
                    help="only run this many eager launches of one workload (for ncu), print nothing")
-    p.add_argument("--profile-workload", choices=["sharded", "b64"], default="sharded")
+    p.add_argument("--profile-workload", choices=["sharded", "b64", "lmhead"], default="sharded")
+    p.add_argument("--lm-steps", type=int, default=1024, help="steps per timed variant of the lm_head leg (0: skip)")
+    p.add_argument("--sweep-steps", type=int, default=512, help="steps per sweep workload (0: skip)")
     p.add_argument("--sweep", action="store_true",
                    help="instead of the headline line: one line per vocabulary-sweep workload (rows x V bf16, "
                         "penalties + top_k 50 + top_p 0.95), device-timed, with its HBM roofline")
@@ -237,6 +239,9 @@ def run_ours(args, dist: Dist):
     if args.profile and args.profile_workload == "b64":
         run_b64(args, device, torch.cuda.Stream(device), dist, profile=args.profile)
         return
+    if args.profile and args.profile_workload == "lmhead":
+        run_lmhead(args, device, torch.cuda.Stream(device), dist, profile=args.profile)
+        return
     start, end = shard_range(PAIRS, dist.world, dist.rank)
     pairs = end - start
     gen = torch.Generator(device).manual_seed(1234 + dist.rank)
@@ -263,7 +268,7 @@ def run_ours(args, dist: Dist):
         torch.cuda.synchronize()
         return
     info = sampler.launch_info(pool[0], history, upool[0])
-    kernel_name = "mtr::row_warp_kernel" if info.kernel == _native.KERNEL_ROW_WARP else "mtr::sampler_kernel"
+    kernel_name = KERNEL_NAMES[info.kernel]
     with ClockSampler(device.index) as clocks:
         ms, graph = time_graph(step, args.steps, stream, dist)
     ms = dist.max(ms)
@@ -300,6 +305,9 @@ def run_ours(args, dist: Dist):
 
     # ---- µs per step of the 64-pair batched decode (latency, per GPU)
     b64 = run_b64(args, device, stream, dist)
+    # ---- the lm_head variant and the sweep (per GPU, same on every rank)
+    lmhead = run_lmhead(args, device, stream, dist) if args.lm_steps > 0 else None
+    sweep = run_sweep_lines(args, device, stream, dist) if args.sweep_steps > 0 else None
 
     cpu = None
     if dist.world == 1 and dist.rank == 0:
@@ -328,6 +336,8 @@ def run_ours(args, dist: Dist):
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
             "decode_step_b64": b64,
+            "lmhead_fused": lmhead,
+            "sweep": sweep,
         }
         print(json.dumps(line), flush=True)
 
@@ -368,6 +378,126 @@ def run_b64(args, device, stream, dist, profile=0):
     return {"us_per_step": ms * 1e3 / steps, "steps": steps, "pairs": pairs,
             "workload": "batched_decode: 64 CFG pairs x V=4096 bf16, CFG 1.5 + monotonic + grammar + "
                         "T=0.9 on time shifts + top_p 0.9, graph-replayed, inputs rotating over > 3x L2"}
+
+
+def run_lmhead(args, device, stream, dist, profile=0):
+    """The lm_head variant: 256 hidden rows (128 CFG pairs) x d=768 bf16 ~ N(0, 1), proj_out weight
+    V=4096 x 768 bf16 ~ N(0, 0.02^2), then the batched-decode chain (CFG 1.5, monotonic, grammar,
+    T=0.9 on time shifts, top_p 0.9, draw).  Times, each over one captured graph of `steps` steps
+    with hidden states and weights rotating over > 3x L2: the tcgen05 projection alone, the
+    projection -> sampler pair (programmatic dependent launch), torch's bf16 matmul (cuBLAS, the
+    reference's nn.Linear) alone and followed by the same sampler, and the sampler alone."""
+    from mapperatorinator_b200.sampling import FusedSampler, GrammarTable, lm_head_logits
+
+    pairs, d = 128, 768
+    gen = torch.Generator(device).manual_seed(99 + dist.rank)
+    class_of, table = make_tables(gen, device)
+    s = FusedSampler(vocab_size=VOCAB, num_rows=pairs, device=device, cfg_scale=1.5, time_shift_range=(0, TS_END),
+                     sos_ids=(SOS_ID,), grammar=GrammarTable.from_bool_table(class_of, table.cpu(), device),
+                     column_temperatures=[(0, TS_END, 0.9)], top_p=0.9)
+    s.mono_state.copy_(torch.randint(0, TS_END, (pairs,), generator=gen, device=device).to(torch.int32))
+    s.prev_token.copy_(torch.randint(0, VOCAB, (pairs,), generator=gen, device=device).to(torch.int32))
+    s._scan_next = s._prev_from_ids_next = False
+    step_bytes = VOCAB * d * 2 + 2 * pairs * d * 2
+    nbuf = math.ceil(3 * L2_BYTES / step_bytes)
+    W = (torch.randn((nbuf, VOCAB, d), generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    H = torch.randn((nbuf, 2 * pairs, d), generator=gen, device=device).to(torch.bfloat16)
+    U = torch.rand((nbuf, pairs), generator=gen, device=device)
+    logits = torch.empty((2 * pairs, VOCAB), dtype=torch.bfloat16, device=device)
+    variants = {
+        "fused": lambda i: s.step_hidden(H[i % nbuf], W[i % nbuf], uniforms=U[i % nbuf]),
+        "projection": lambda i: lm_head_logits(H[i % nbuf], W[i % nbuf], out=logits),
+        "cublas_then_sampler": lambda i: (torch.matmul(H[i % nbuf], W[i % nbuf].T, out=logits),
+                                          s.step(logits, uniforms=U[i % nbuf])),
+        "cublas": lambda i: torch.matmul(H[i % nbuf], W[i % nbuf].T, out=logits),
+        "sampler": lambda i: s.step(logits, uniforms=U[i % nbuf]),
+    }
+    with torch.cuda.stream(stream):
+        for fn in variants.values():
+            for i in range(8):
+                fn(i)
+    torch.cuda.synchronize()
+    if profile:
+        with torch.cuda.stream(stream):
+            for i in range(profile):
+                variants["fused"](i)
+        torch.cuda.synchronize()
+        return None
+    steps = args.lm_steps
+    us = {}
+    for name, fn in variants.items():
+        ms, g = time_graph(fn, steps, stream, dist)
+        us[name] = dist.max(ms) * 1e3 / steps
+        del g
+    flops = 2.0 * 2 * pairs * VOCAB * d
+    tflops = flops / (us["projection"] * 1e-6) / 1e12
+    try:
+        peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+        peak_kind = "measured (burst)"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
+    return {"workload": "lmhead: 256 hidden rows (128 CFG pairs) x d=768 bf16 -> V=4096 bf16 logits (tcgen05) "
+                        "-> CFG 1.5 + monotonic + grammar + T=0.9 on time shifts + top_p 0.9 + draw",
+            "us_per_step": us["fused"], "tokens_per_s": pairs / (us["fused"] * 1e-6),
+            "us": {k: round(v, 3) for k, v in us.items()},
+            "projection_roofline": {"bound": "tensor", "achieved": tflops, "peak": peak, "unit": "TFLOP/s",
+                                    "frac": tflops / peak, "peak_kind": peak_kind, "flops_per_launch": flops,
+                                    "kernel": "mtr::lm::lmhead_gemm_kernel"},
+            "speedup_vs_cublas_then_sampler": us["cublas_then_sampler"] / us["fused"],
+            "steps": steps, "l2": f"hidden + weights rotate over {nbuf} sets ({nbuf * step_bytes / 2**20:.0f} MiB)"}
+
+
+def run_sweep_lines(args, device, stream, dist):
+    """The throughput sweep (rows x V bf16 N(0, 2^2), 512-id history, repetition 1.1 / frequency 0.2 /
+    presence 0.1, top_k 50, top_p 0.95, draw) and the reference's production preset (temperature
+    0.9, top_p 0.9, no top_k) at 1024 x 4096: one dict per workload, device-timed."""
+    from mapperatorinator_b200 import _native
+    from mapperatorinator_b200.sampling import FusedSampler
+
+    peak, peak_kind = measured_peak()
+    out = []
+    cases = [(rows, vocab, "penalties_topk50_topp0.95") for rows, vocab in SWEEP] + [(1024, 4096, "T0.9_topp0.9")]
+    for rows, vocab, chain in cases:
+        gen = torch.Generator(device).manual_seed(4321 + rows + vocab)
+        if chain == "T0.9_topp0.9":
+            s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, temperature=0.9, top_p=0.9)
+            hist = None
+        else:
+            s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, repetition_penalty=1.1,
+                             frequency_penalty=0.2, presence_penalty=0.1, top_k=50, top_p=0.95)
+            hist = torch.randint(0, vocab, (rows, HISTORY), generator=gen, device=device)
+        buf_bytes = rows * vocab * 2
+        nbuf = max(4, math.ceil(3 * L2_BYTES / buf_bytes))
+        pool = [(torch.randn((rows, vocab), generator=gen, device=device) * 2.0).to(torch.bfloat16)
+                for _ in range(nbuf)]
+        upool = torch.rand((nbuf, rows), generator=gen, device=device)
+
+        def step(i, s=s, pool=pool, upool=upool, hist=hist, nbuf=nbuf):
+            s.step(pool[i % nbuf], hist, uniforms=upool[i % nbuf])
+
+        with torch.cuda.stream(stream):
+            for i in range(max(3, args.warmup)):
+                step(i)
+        torch.cuda.synchronize()
+        info = s.launch_info(pool[0], hist, upool[0])
+        steps = args.sweep_steps
+        ms, graph = time_graph(step, steps, stream, dist)
+        ms = dist.max(ms)
+        del graph
+        us = ms * 1e3 / steps
+        nbytes = rows * vocab * 2 + (rows * HISTORY * 8 if hist is not None else 0) + rows * (4 + 8 + 4)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out.append({"rows": rows, "vocab": vocab, "chain": chain, "us_per_step": round(us, 3),
+                    "tokens_per_s": rows / (us * 1e-6), "algorithmic_bytes_per_launch": nbytes,
+                    "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+                    "kernel": KERNEL_NAMES[info.kernel], "grid": info.grid, "threads": info.threads,
+                    "cluster": info.cluster_size, "l2": f"logits rotate over {nbuf} buffers"})
+        del s, pool, upool, hist
+        torch.cuda.empty_cache()
+    return out
+
+
+KERNEL_NAMES = {0: "mtr::sampler_kernel", 1: "mtr::row_warp_kernel", 2: "mtr::stream_kernel"}
 
 
 # ---------------------------------------------------------------- CPU side
@@ -509,7 +639,7 @@ def run_sweep(args, dist):
         us = ms * 1e3 / steps
         nbytes = rows * vocab * 2 + rows * HISTORY * 8 + rows * (4 + 8 + 4)
         gbs = nbytes / (us * 1e-6) / 1e9
-        kernel = "mtr::row_warp_kernel" if info.kernel == _native.KERNEL_ROW_WARP else "mtr::sampler_kernel"
+        kernel = KERNEL_NAMES[info.kernel]
         if dist.rank == 0:
             print(json.dumps({"workload": "vocab_sweep", "rows": rows, "vocab": vocab, "rows_x_vocab": rows * vocab,
                               "us_per_step": us, "tokens_per_s": rows / (us * 1e-6), "steps": steps,

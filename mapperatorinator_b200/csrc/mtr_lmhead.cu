@@ -68,11 +68,12 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 // Waits for the phase with parity `ph` to complete; false after `budget_ns`
-// nanoseconds (0: a single poll).
+// nanoseconds (0: a single poll).  The clock is read only every 4096 polls:
+// a healthy hand-off completes long before the first read.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t ph, uint64_t budget_ns) {
   const uint32_t a = smem_u32(b);
   uint64_t t0 = 0;
-  for (uint32_t i = 0;; ++i) {
+  for (uint32_t i = 1;; ++i) {
     uint32_t done;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -83,7 +84,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t ph, uint64_t bud
         : "memory");
     if (done) return true;
     if (budget_ns == 0) return false;
-    if ((i & 255u) == 0u) {
+    if ((i & 4095u) == 0u) {
       const uint64_t t = global_ns();
       if (t0 == 0) t0 = t;
       else if (t - t0 > budget_ns) return false;
@@ -96,9 +97,6 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
           smem_u32(dst)),
       "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
-}
-__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -158,6 +156,11 @@ __global__ void __launch_bounds__(128, 1)
   auto a_tile = [&](int s) { return ring + (size_t)s * RG::STAGE_BYTES; };
   auto b_tile = [&](int s) { return ring + (size_t)s * RG::STAGE_BYTES + RG::A_BYTES; };
 
+  // the producer (thread 0) initialises the barriers and issues the first ring
+  // stages at once: the loads need no tensor memory, so they overlap its
+  // allocation and the setup barrier
+  const int KB = p.kblocks;
+  const int first = KB < S ? KB : S;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
@@ -167,8 +170,11 @@ __global__ void __launch_bounds__(128, 1)
     abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    prefetch_map(&map_h);
-    prefetch_map(&map_w);
+    for (int kb = 0; kb < first; ++kb) {
+      mbar_expect_tx(&full[kb], RG::STAGE_BYTES);
+      tma_load_2d(a_tile(kb), &map_h, kb * BK, m0, &full[kb]);
+      tma_load_2d(b_tile(kb), &map_w, kb * BK, n0, &full[kb]);
+    }
   }
   if (warp == 2) {  // the whole warp allocates; BN is a power of two >= 32
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_slot)),
@@ -180,12 +186,11 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  const int KB = p.kblocks;
 
   if (warp == 0 && lane == 0) {
-    // ---------------- producer
-    int issued = 0;
-    for (int kb = 0; kb < KB; ++kb) {
+    // ---------------- producer (the first `first` stages are in flight already)
+    int issued = first;
+    for (int kb = first; kb < KB; ++kb) {
       const int s = kb % S;
       if (kb >= S && !mbar_wait(&empty[s], ((kb / S) & 1) ^ 1, WAIT_NS)) {
         abort_flag = 1u;
@@ -224,8 +229,11 @@ __global__ void __launch_bounds__(128, 1)
   }
   __syncwarp();
 
-  // ---------------- epilogue: all four warps
-  const bool waited = mbar_wait(&done, 0, WAIT_NS);
+  // ---------------- epilogue: all four warps; one lane per warp polls the
+  // barrier (128 pollers would contend with the copies' completions for it)
+  bool waited = true;
+  if (lane == 0) waited = mbar_wait(&done, 0, WAIT_NS);
+  waited = __shfl_sync(FULL, waited, 0) != 0;
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   tc_fence_after();
   // tcgen05.ld is warp-collective: the whole warp reads or none of it

@@ -56,12 +56,17 @@ def test_projection_within_float64_bound(cuda_device, rows, d, vocab, tile_n):
 
 
 def test_projection_against_cublas(cuda_device):
+    # cuBLAS (the reference's proj_out) and the tcgen05 kernel accumulate in
+    # different orders: both meet the same float64 bound, so they differ by at
+    # most twice it, and they agree on almost every logit
     h, w = _inputs(cuda_device, 256, 768, 4096, seed=5)
     out = S.lm_head_logits(h, w)
-    ref = h @ w.T  # the reference's proj_out on cuBLAS, bf16 out
+    ref = h @ w.T
     torch.cuda.synchronize()
-    diff = (out.float() - ref.float()).abs()
-    assert bool((diff <= _bf16_ulp(ref.float()) * 1.0001).all())
+    exact = h.double() @ w.double().T
+    bound = 0.5 * _bf16_ulp(exact) * (1 + 2.0 ** -7) + 768 * 2.0 ** -24 * (h.double().abs() @ w.double().abs().T)
+    assert bool(((ref.double() - exact).abs() <= bound).all())
+    assert bool(((out.double() - ref.double()).abs() <= 2 * bound).all())
     assert float((out != ref).double().mean()) < 0.01
 
 
