@@ -326,6 +326,10 @@ int mtr_sampler_query_args(const MtrSamplerArgs* args, MtrLaunchInfo* out);
  * Validate and enqueue the fused step on `stream` (a cudaStream_t; NULL = the
  * legacy default stream).  The current CUDA device must own every pointer.
  * Returns MTR_OK once the kernel is enqueued.  Capturable in a CUDA graph.
+ * The kernel is a programmatic dependent launch: its CTAs may be scheduled
+ * while the previous kernel on the stream runs, and wait at entry until that
+ * kernel has completed with its memory visible (stream order is unchanged;
+ * only launch latency overlaps).
  */
 int mtr_sampler_launch(const MtrSamplerArgs* args, void* stream);
 

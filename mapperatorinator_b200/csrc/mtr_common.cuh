@@ -523,8 +523,16 @@ inline unsigned launch_attrs(cudaLaunchAttribute* at, int cs, bool pdl) {
   return n;
 }
 
-// Kernel entry: when launched as a programmatic dependent, wait for the
-// previous grid's results (a no-op otherwise).
+// Kernel entry of every sampler kernel: wait for the previous grid on the
+// stream to complete with its memory visible (a no-op unless this launch is a
+// programmatic dependent).
 __device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Let the next programmatic dependent launch: its CTAs may be scheduled while
+// this grid runs and wait at their own entry, so only launch latency overlaps,
+// never data.  The row-per-CTA kernel calls it at entry; the persistent kernels
+// do not (their early-finishing CTAs' slots would fill with waiting CTAs beside
+// the last rows' warps), so their dependents launch as they exit.
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 }  // namespace mtr

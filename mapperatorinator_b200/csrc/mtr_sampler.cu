@@ -162,6 +162,59 @@ __device__ __forceinline__ void find_topp_crossing(WF w, float top_p, int top_p_
   __syncthreads();
 }
 
+// The same result with every warp of the CTA: warp w sums bins w*PW ..
+// (NBINS/THREADS per lane), the warp totals go through shared memory (`wtot`,
+// NW entries), and every warp scans them to find the crossing warp, whose lane
+// then resolves its bins.  Two barriers instead of one, but no warp walks more
+// than NBINS/THREADS bins.
+template <int NBINS, int THREADS, typename WF>
+__device__ __forceinline__ void find_topp_crossing_blk(WF w, float top_p, int top_p_mode, Cross* out, u64* plim_out,
+                                                       u64* wtot) {
+  constexpr int NW = THREADS / 32, BPL = NBINS / THREADS;
+  static_assert(NBINS % THREADS == 0 && NW <= 32, "bins per lane");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b0 = tid * BPL;  // this lane's bins, in order
+  u64 wb[BPL], s = 0;
+#pragma unroll
+  for (int i = 0; i < BPL; ++i) {
+    wb[i] = w(b0 + i);
+    s += wb[i];
+  }
+  const u64 incl = warp_incl_scan_u64(s, lane);
+  if (lane == 31) wtot[warp] = incl;
+  __syncthreads();
+  const u64 wv = lane < NW ? wtot[lane] : 0ull;
+  const u64 winc = warp_incl_scan_u64(wv, lane);
+  const u64 total = __shfl_sync(FULL, winc, NW - 1);
+  const u64 wbase = __shfl_sync(FULL, winc - wv, warp);
+  const double P = __dmul_rn((double)top_p, (double)total);
+  const u64 lim = top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+  if (tid == 0) {
+    *plim_out = lim;
+    out->total = total;
+  }
+  const u64 lo = wbase + incl - s;
+  bool none = !(lim < total);
+  if (!none && lo <= lim && lim < lo + s) {  // exactly one lane holds the crossing
+    u64 a = lo;
+#pragma unroll
+    for (int i = 0; i < BPL; ++i) {
+      if (a <= lim && lim < a + wb[i]) {
+        out->bin = b0 + i;
+        out->above = a;
+        out->w = wb[i];
+      }
+      a += wb[i];
+    }
+  }
+  if (tid == 0 && none) {
+    out->bin = -1;
+    out->above = total;
+    out->w = 0;
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // shared memory
 // ---------------------------------------------------------------------------
@@ -186,6 +239,7 @@ struct alignas(16) Shared {
   uint32_t status;    // bits raised while processing this CTA's tile
   uint32_t status_g;  // grammar lookups
   uint32_t status_u;  // uniform
+  uint32_t warm;      // see the parameter warm-up in the prologue
   int32_t n_uniq;
   int32_t nc;         // local candidate count
   int32_t nm;         // crossing-bin list count
@@ -276,6 +330,7 @@ template <typename Tin, int THREADS, int EPT, int CS>
 __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
     sampler_kernel(const __grid_constant__ MtrSamplerArgs a, const __grid_constant__ Derived dv) {
   wait_prior_grid();
+  allow_dependents();
   using E = Elem<Tin>;
   constexpr int VEC = E::VEC;
   constexpr int NCH = EPT / VEC;
@@ -436,6 +491,13 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
         sm.lb_timed = timed;
         sm.lb_p = a.lb_state[row];
       }
+    } else if (warp == 6) {
+      // first touches of the parameter lines only the epilogue reads: done here,
+      // they overlap the prologue instead of missing the constant cache one after
+      // another in the row's serial tail
+      sm.warm = (uint32_t)a.n_eos_ranges + (uint32_t)a.lookback_mode + (uint32_t)(a.stop_counts != nullptr) +
+                (uint32_t)(a.id_buffer != nullptr) + (uint32_t)a.n_eos + (uint32_t)(a.unfinished != nullptr) +
+                (uint32_t)(a.out_status != nullptr) + (uint32_t)a.pad_id;
     } else if (warp == 4) {
       sm.status = 0u;
       sm.n_uniq = 0;
@@ -1333,8 +1395,8 @@ __global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? 2 : 1))
           Clu<CS>::sync();
           // total, the limit it implies, and the crossing of the limit, in one pass
           if constexpr (CS == 1) {
-            find_topp_crossing<NB>([&](int i) -> u64 { return (u64)hlo[i] + ((u64)hhi[i] << 16); }, a.top_p,
-                                   a.top_p_mode, &sm.cr, &sm.plim);
+            find_topp_crossing_blk<NB, THREADS>([&](int i) -> u64 { return (u64)hlo[i] + ((u64)hhi[i] << 16); },
+                                                a.top_p, a.top_p_mode, &sm.cr, &sm.plim, sm.wl);
           } else {
             for (int i = tid; i < NB; i += THREADS) {
               u64 m = 0;
@@ -3707,7 +3769,7 @@ int mtr_sampler_launch(const MtrSamplerArgs* a, void* stream) {
   const int v = mtr::validate_all(a);
   if (v != MTR_OK) return v;
   if (a->num_rows == 0) return MTR_OK;
-  return mtr::sampler_launch(a, (cudaStream_t)stream, false);
+  return mtr::sampler_launch(a, (cudaStream_t)stream, true);
 }
 
 }  // extern "C"
