@@ -60,7 +60,7 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--profile", type=int, default=0,
                    help="only run this many eager launches of one workload (for ncu), print nothing")
-    p.add_argument("--profile-workload", choices=["sharded", "b64", "lmhead"], default="sharded")
+    p.add_argument("--profile-workload", choices=["sharded", "b64", "lmhead", "v65536", "topp1024"], default="sharded")
     p.add_argument("--lm-steps", type=int, default=1024, help="steps per timed variant of the lm_head leg (0: skip)")
     p.add_argument("--sweep-steps", type=int, default=512, help="steps per sweep workload (0: skip)")
     p.add_argument("--sweep", action="store_true",
@@ -241,6 +241,10 @@ def run_ours(args, dist: Dist):
         return
     if args.profile and args.profile_workload == "lmhead":
         run_lmhead(args, device, torch.cuda.Stream(device), dist, profile=args.profile)
+        return
+    if args.profile and args.profile_workload in ("v65536", "topp1024"):
+        rows, vocab, chain = (256, 65536, "penalties") if args.profile_workload == "v65536" else (1024, 4096, "topp")
+        run_sweep_case(args, device, torch.cuda.Stream(device), dist, rows, vocab, chain, profile=args.profile)
         return
     start, end = shard_range(PAIRS, dist.world, dist.rank)
     pairs = end - start
@@ -451,50 +455,57 @@ def run_sweep_lines(args, device, stream, dist):
     """The throughput sweep (rows x V bf16 N(0, 2^2), 512-id history, repetition 1.1 / frequency 0.2 /
     presence 0.1, top_k 50, top_p 0.95, draw) and the reference's production preset (temperature
     0.9, top_p 0.9, no top_k) at 1024 x 4096: one dict per workload, device-timed."""
-    from mapperatorinator_b200 import _native
+    out = []
+    cases = [(rows, vocab, "penalties") for rows, vocab in SWEEP] + [(1024, 4096, "topp")]
+    for rows, vocab, chain in cases:
+        out.append(run_sweep_case(args, device, stream, dist, rows, vocab, chain))
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_sweep_case(args, device, stream, dist, rows, vocab, chain, profile=0):
+    """One sweep workload: `chain` "penalties" = repetition 1.1 / frequency 0.2 / presence 0.1 + top_k 50 +
+    top_p 0.95 over a 512-id history; "topp" = temperature 0.9 + top_p 0.9 (the reference's production
+    preset).  Logits rotate over > 3x L2.  With `profile`, only runs that many eager launches."""
     from mapperatorinator_b200.sampling import FusedSampler
 
     peak, peak_kind = measured_peak()
-    out = []
-    cases = [(rows, vocab, "penalties_topk50_topp0.95") for rows, vocab in SWEEP] + [(1024, 4096, "T0.9_topp0.9")]
-    for rows, vocab, chain in cases:
-        gen = torch.Generator(device).manual_seed(4321 + rows + vocab)
-        if chain == "T0.9_topp0.9":
-            s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, temperature=0.9, top_p=0.9)
-            hist = None
-        else:
-            s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, repetition_penalty=1.1,
-                             frequency_penalty=0.2, presence_penalty=0.1, top_k=50, top_p=0.95)
-            hist = torch.randint(0, vocab, (rows, HISTORY), generator=gen, device=device)
-        buf_bytes = rows * vocab * 2
-        nbuf = max(4, math.ceil(3 * L2_BYTES / buf_bytes))
-        pool = [(torch.randn((rows, vocab), generator=gen, device=device) * 2.0).to(torch.bfloat16)
-                for _ in range(nbuf)]
-        upool = torch.rand((nbuf, rows), generator=gen, device=device)
+    gen = torch.Generator(device).manual_seed(4321 + rows + vocab)
+    if chain == "topp":
+        s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, temperature=0.9, top_p=0.9)
+        hist = None
+    else:
+        s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, repetition_penalty=1.1,
+                         frequency_penalty=0.2, presence_penalty=0.1, top_k=50, top_p=0.95)
+        hist = torch.randint(0, vocab, (rows, HISTORY), generator=gen, device=device)
+    buf_bytes = rows * vocab * 2
+    nbuf = max(4, math.ceil(3 * L2_BYTES / buf_bytes))
+    pool = [(torch.randn((rows, vocab), generator=gen, device=device) * 2.0).to(torch.bfloat16) for _ in range(nbuf)]
+    upool = torch.rand((nbuf, rows), generator=gen, device=device)
 
-        def step(i, s=s, pool=pool, upool=upool, hist=hist, nbuf=nbuf):
-            s.step(pool[i % nbuf], hist, uniforms=upool[i % nbuf])
+    def step(i):
+        s.step(pool[i % nbuf], hist, uniforms=upool[i % nbuf])
 
-        with torch.cuda.stream(stream):
-            for i in range(max(3, args.warmup)):
-                step(i)
-        torch.cuda.synchronize()
-        info = s.launch_info(pool[0], hist, upool[0])
-        steps = args.sweep_steps
-        ms, graph = time_graph(step, steps, stream, dist)
-        ms = dist.max(ms)
-        del graph
-        us = ms * 1e3 / steps
-        nbytes = rows * vocab * 2 + (rows * HISTORY * 8 if hist is not None else 0) + rows * (4 + 8 + 4)
-        gbs = nbytes / (us * 1e-6) / 1e9
-        out.append({"rows": rows, "vocab": vocab, "chain": chain, "us_per_step": round(us, 3),
-                    "tokens_per_s": rows / (us * 1e-6), "algorithmic_bytes_per_launch": nbytes,
-                    "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
-                    "kernel": KERNEL_NAMES[info.kernel], "grid": info.grid, "threads": info.threads,
-                    "cluster": info.cluster_size, "l2": f"logits rotate over {nbuf} buffers"})
-        del s, pool, upool, hist
-        torch.cuda.empty_cache()
-    return out
+    with torch.cuda.stream(stream):
+        for i in range(max(3, args.warmup) + profile):
+            step(i)
+    torch.cuda.synchronize()
+    if profile:
+        return None
+    info = s.launch_info(pool[0], hist, upool[0])
+    steps = args.sweep_steps
+    ms, graph = time_graph(step, steps, stream, dist)
+    ms = dist.max(ms)
+    del graph
+    us = ms * 1e3 / steps
+    nbytes = rows * vocab * 2 + (rows * HISTORY * 8 if hist is not None else 0) + rows * (4 + 8 + 4)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"rows": rows, "vocab": vocab,
+            "chain": "penalties_topk50_topp0.95" if chain == "penalties" else "T0.9_topp0.9",
+            "us_per_step": round(us, 3), "tokens_per_s": rows / (us * 1e-6), "algorithmic_bytes_per_launch": nbytes,
+            "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+            "kernel": KERNEL_NAMES[info.kernel], "grid": info.grid, "threads": info.threads,
+            "cluster": info.cluster_size, "l2": f"logits rotate over {nbuf} buffers"}
 
 
 KERNEL_NAMES = {0: "mtr::sampler_kernel", 1: "mtr::row_warp_kernel", 2: "mtr::stream_kernel"}
@@ -603,53 +614,17 @@ SWEEP = ((256, 4096), (256, 16384), (256, 65536), (1024, 4096))
 
 
 def run_sweep(args, dist):
-    """rows x V bf16 logits N(0, 2^2), 512-id int64 history uniform over V, repetition 1.1 / frequency 0.2 /
-    presence 0.1, top_k 50, top_p 0.95, inverse-CDF draw; no CFG.  One line per (rows, V)."""
+    """`--sweep`: one JSON line per sweep workload instead of the headline line."""
     from mapperatorinator_b200 import _native
-    from mapperatorinator_b200.sampling import FusedSampler
 
     _native.load()  # fail loudly without the native library
     device = torch.device("cuda", dist.local)
     torch.cuda.set_device(device)
     stream = torch.cuda.Stream(device)
-    peak, peak_kind = measured_peak()
-    for rows, vocab in SWEEP:
-        gen = torch.Generator(device).manual_seed(4321 + rows + vocab)
-        s = FusedSampler(vocab_size=vocab, num_rows=rows, device=device, repetition_penalty=1.1,
-                         frequency_penalty=0.2, presence_penalty=0.1, top_k=50, top_p=0.95)
-        hist = torch.randint(0, vocab, (rows, HISTORY), generator=gen, device=device)
-        buf_bytes = rows * vocab * 2
-        nbuf = max(4, math.ceil(3 * L2_BYTES / buf_bytes))
-        pool = [(torch.randn((rows, vocab), generator=gen, device=device) * 2.0).to(torch.bfloat16)
-                for _ in range(nbuf)]
-        upool = torch.rand((nbuf, rows), generator=gen, device=device)
-
-        def step(i, s=s, pool=pool, upool=upool, hist=hist, nbuf=nbuf):
-            s.step(pool[i % nbuf], hist, uniforms=upool[i % nbuf])
-
-        with torch.cuda.stream(stream):
-            for i in range(max(3, args.warmup)):
-                step(i)
-        torch.cuda.synchronize()
-        info = s.launch_info(pool[0], hist, upool[0])
-        steps = max(64, min(args.steps, 2048))
-        ms, graph = time_graph(step, steps, stream, dist)
-        ms = dist.max(ms)
-        del graph
-        us = ms * 1e3 / steps
-        nbytes = rows * vocab * 2 + rows * HISTORY * 8 + rows * (4 + 8 + 4)
-        gbs = nbytes / (us * 1e-6) / 1e9
-        kernel = KERNEL_NAMES[info.kernel]
+    args.sweep_steps = max(64, min(args.steps, 2048))
+    for line in run_sweep_lines(args, device, stream, dist):
         if dist.rank == 0:
-            print(json.dumps({"workload": "vocab_sweep", "rows": rows, "vocab": vocab, "rows_x_vocab": rows * vocab,
-                              "us_per_step": us, "tokens_per_s": rows / (us * 1e-6), "steps": steps,
-                              "algorithmic_bytes_per_launch": nbytes, "achieved_gbs": gbs, "peak_gbs": peak,
-                              "frac": gbs / peak, "peak_kind": peak_kind, "kernel": kernel, "grid": info.grid,
-                              "threads": info.threads, "cluster": info.cluster_size,
-                              "l2": f"logits rotate over {nbuf} buffers ({nbuf * buf_bytes / 2**20:.0f} MiB)"}),
-                  flush=True)
-        del s, pool, upool, hist
-        torch.cuda.empty_cache()
+            print(json.dumps(dict(line, workload="vocab_sweep")), flush=True)
 
 
 def main():
