@@ -2095,6 +2095,252 @@ __device__ __forceinline__ void load_ahead(const MtrSamplerArgs& a, const Derive
   }
 }
 
+// Result of the row-per-warp kernel's dense mass path.
+struct WDense {
+  float cut_x;
+  int32_t cut_id;
+  u64 qkept;
+  int32_t token;
+  uint32_t status;
+  int32_t topp_cut;
+  int32_t ok;  // 0: a crossing bin still held more than WMINI candidates after refinement
+};
+
+// Top-p and the draw over every score of a staged row when there is no
+// survivor list (no top-k, or more survivors than the list holds).  Pass A
+// computes the fixed-point mass q of every score >= tk and, with top-p, adds it
+// to a histogram of the distance to the max in 1/16-logit bins (monotone in the
+// score, so bins follow canonical order); warp_crossing_halves finds the bin
+// holding the limit.  Its candidates are listed (a second 256-bin level splits
+// the bin when it holds more than WMINI) and resolved in canonical order (score
+// descending, id ascending).  The draw walks the 16 id slots of 256 ids in id
+// order, one warp scan of the kept masses per slot, and stops in the slot that
+// crosses floor(u * Q_kept).  X holds the row as the kernel stages it: chunk c
+// (ids 8c .. 8c+7) at lo(c) and hi(c).
+template <bool SPLIT>
+__device__ __noinline__ void warp_dense(const float* X, int HALF, int nch, int V, float gmax, float tk, bool topp_on,
+                                        float top_p, int top_p_mode, bool sample, float u, uint32_t* hlo, float* mx,
+                                        int32_t* mi, uint32_t* mq, int lane, WDense* out) {
+  constexpr int NS = WV_MAX / 256;
+  uint32_t* const hhi = hlo + WNB;
+  auto lo_of = [&](int c) -> const float* { return X + (SPLIT ? 4 * c : 8 * c); };
+  auto hi_of = [&](int c) -> const float* { return X + (SPLIT ? HALF + 4 * c : 8 * c + 4); };
+  auto load8 = [&](int c, float (&v)[8]) {
+    const float4 f0 = *(const float4*)lo_of(c), f1 = *(const float4*)hi_of(c);
+    v[0] = f0.x; v[1] = f0.y; v[2] = f0.z; v[3] = f0.w;
+    v[4] = f1.x; v[5] = f1.y; v[6] = f1.z; v[7] = f1.w;
+  };
+  // fixed-point masses of chunk c's scores that take part (finite, >= tk, id < V)
+  auto mass8 = [&](int c, const float (&v)[8], uint32_t (&q)[8]) {
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) expfx2(__fsub_rn(v[e], gmax), __fsub_rn(v[e + 1], gmax), q[e], q[e + 1]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (!(finite_val(v[e]) && v[e] >= tk) || 8 * c + e >= V) q[e] = 0u;
+  };
+  auto bin1 = [&](float x) -> int {
+    return __float2int_rz(fminf(__fmul_rn(__fsub_rn(gmax, x), 16.0f), (float)(WNB - 1)));
+  };
+  auto zero_hist = [&]() {
+#pragma unroll
+    for (int i = lane * 4; i < 2 * WNB; i += 128) *(uint4*)(hlo + i) = make_uint4(0u, 0u, 0u, 0u);
+    __syncwarp();
+  };
+  out->ok = 1;
+  out->status = 0;
+  out->topp_cut = 0;
+  out->cut_x = 0.0f;
+  out->cut_id = NO_ID;
+  out->token = -1;
+
+  // ---- pass A: total mass (and the level-1 histogram)
+  if (topp_on) zero_hist();
+  u64 tot = 0;
+#pragma unroll 1
+  for (int s = 0; s < NS; ++s) {
+    const int c = s * 32 + lane;
+    if (c >= nch) break;
+    float v[8];
+    uint32_t q[8];
+    load8(c, v);
+    mass8(c, v, q);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      tot += q[e];
+      if (topp_on && q[e]) {
+        const int b = bin1(v[e]);
+        atomicAdd(hlo + b, q[e] & 0xffffu);
+        atomicAdd(hhi + b, q[e] >> 16);
+      }
+    }
+  }
+  tot = warp_sum_u64(tot);
+  u64 qkept = tot;
+
+  if (topp_on) {
+    const double P = __dmul_rn((double)top_p, (double)tot);
+    const u64 plim = top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+    __syncwarp();
+    u64 above, w;
+    const int b1 = max(warp_crossing_halves(hlo, hhi, plim, lane, above, w), 0);  // plim < total
+    // level 2 (only when bin b1 lists too many): 256 sub-bins of its distance range
+    const float dlo = (float)b1 * (1.0f / 16.0f);
+    const float dw = b1 < WNB - 1 ? (1.0f / 16.0f) : 24.0f - dlo;  // the overflow bin: q = 0 beyond 21.5
+    const float sub_scale = (float)WNB / dw;
+    auto bin2 = [&](float x) -> int {
+      const float z = __fmul_rn(__fsub_rn(__fsub_rn(gmax, x), dlo), sub_scale);
+      return __float2int_rz(fminf(fmaxf(z, 0.0f), (float)(WNB - 1)));
+    };
+    int level = 1, b2 = -1;
+    int m = 0;
+#pragma unroll 1
+    while (true) {
+      // list the candidates of the crossing bin (of sub-bin b2 at level 2)
+      m = 0;
+#pragma unroll 1
+      for (int s = 0; s < NS; ++s) {
+        const int c = s * 32 + lane;
+        float v[8];
+        uint32_t memb = 0;
+        if (c < nch) {
+          load8(c, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            memb |= (uint32_t)(finite_val(v[e]) && v[e] >= tk && 8 * c + e < V && bin1(v[e]) == b1 &&
+                               (level == 1 || bin2(v[e]) == b2)) << e;
+        }
+        const uint32_t cnt = __popc(memb);
+        const uint32_t incl = warp_incl_scan_u32(cnt, lane);
+        int pos = m + (int)(incl - cnt);
+        if (memb) {
+          uint32_t q[8];
+          mass8(c, v, q);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if ((memb >> e) & 1u) {
+              if (pos < WMINI) {
+                mx[pos] = v[e];
+                mi[pos] = 8 * c + e;
+                mq[pos] = q[e];
+              }
+              ++pos;
+            }
+        }
+        m += (int)__shfl_sync(FULL, incl, 31);
+      }
+      __syncwarp();
+      if (m <= WMINI) break;
+      if (level == 2) {
+        out->ok = 0;  // the radix path takes the row
+        return;
+      }
+      // split bin b1 into 256 sub-bins of its distance range
+      zero_hist();
+#pragma unroll 1
+      for (int s = 0; s < NS; ++s) {
+        const int c = s * 32 + lane;
+        if (c >= nch) break;
+        float v[8];
+        load8(c, v);
+        uint32_t memb = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          memb |= (uint32_t)(finite_val(v[e]) && v[e] >= tk && 8 * c + e < V && bin1(v[e]) == b1) << e;
+        if (memb) {
+          uint32_t q[8];
+          mass8(c, v, q);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            if (((memb >> e) & 1u) && q[e]) {
+              const int b = bin2(v[e]);
+              atomicAdd(hlo + b, q[e] & 0xffffu);
+              atomicAdd(hhi + b, q[e] >> 16);
+            }
+        }
+      }
+      __syncwarp();
+      u64 above2, w2;
+      b2 = max(warp_crossing_halves(hlo, hhi, plim - above, lane, above2, w2), 0);  // plim - above < w
+      above += above2;
+      level = 2;
+    }
+    // canonical order inside the final bin: the candidate whose mass prefix crosses plim
+    float my_x = 0.0f;
+    int32_t my_id = NO_ID;
+    u64 my_q = 0;
+    bool found = false;
+#pragma unroll 1
+    for (int j = lane; j < m; j += 32) {
+      const float xj = mx[j];
+      const int32_t ij = mi[j];
+      u64 am = above;
+#pragma unroll 1
+      for (int jj = 0; jj < m; ++jj)
+        if (canon_before(mx[jj], mi[jj], xj, ij)) am += mq[jj];
+      if (mq[j] != 0u && am <= plim && am + mq[j] > plim) {
+        my_x = xj;
+        my_id = ij;
+        my_q = am + mq[j];
+        found = true;
+      }
+    }
+    const unsigned bf = __ballot_sync(FULL, found);
+    const int src = max(__ffs(bf) - 1, 0);
+    out->cut_x = __shfl_sync(FULL, my_x, src);
+    out->cut_id = __shfl_sync(FULL, my_id, src);
+    qkept = __shfl_sync(FULL, my_q, src);
+    out->topp_cut = 1;
+    bool tie = false;
+#pragma unroll 1
+    for (int j = lane; j < m; j += 32) tie |= mx[j] == out->cut_x && mi[j] > out->cut_id;
+    if (__any_sync(FULL, tie)) out->status |= MTR_ROW_TIE_AT_CUT;
+    __syncwarp();
+  }
+  out->qkept = qkept;
+
+  // ---- the draw: id slots in order, one warp scan of the kept masses per slot
+  if (sample) {
+    const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
+    const bool cut = out->topp_cut != 0;
+    const float cx = out->cut_x;
+    const int32_t cid = out->cut_id;
+    u64 run = 0;
+    int32_t tok = NO_ID;
+#pragma unroll 1
+    for (int s = 0; s < NS; ++s) {
+      const int c = s * 32 + lane;
+      uint32_t q[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+      u64 cs = 0;
+      if (c < nch) {
+        float v[8];
+        load8(c, v);
+        mass8(c, v, q);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          if (cut && !(v[e] > cx || (v[e] == cx && 8 * c + e <= cid))) q[e] = 0u;
+          cs += q[e];
+        }
+      }
+      const u64 incl = warp_incl_scan_u64(cs, lane);
+      const u64 tsum = __shfl_sync(FULL, incl, 31);
+      if (run + tsum > R) {
+        const u64 lo = run + incl - cs;
+        if (cs != 0 && lo <= R && R < lo + cs) {
+          u64 acc = lo;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            acc += q[e];
+            if (tok == NO_ID && acc > R) tok = 8 * c + e;
+          }
+        }
+        break;
+      }
+      run += tsum;
+    }
+    out->token = __reduce_min_sync(FULL, tok);
+  }
+}
+
 template <typename Tin, bool CFG>
 __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant__ MtrSamplerArgs a,
                                                          const __grid_constant__ Derived dv) {
@@ -3175,8 +3421,24 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
         }
         token = __reduce_min_sync(FULL, my_tok);
       }
+    } else if (need_mass && !force_radix &&
+               [&]() {
+                 WDense dr;
+                 warp_dense<SPLIT>(X, HALF, nch, V, gmax, tk, dv.topp_on != 0, a.top_p, a.top_p_mode,
+                                   sel == MTR_SELECT_SAMPLE, u, (uint32_t*)hist, mx, mi, mq, lane, &dr);
+                 if (!dr.ok) return false;
+                 cut_x = dr.cut_x;
+                 cut_id = dr.cut_id;
+                 qkept = dr.qkept;
+                 topp_cut = dr.topp_cut != 0;
+                 status |= dr.status;
+                 if (sel == MTR_SELECT_SAMPLE) token = dr.token;
+                 return true;
+               }()) {
+      // the dense mass path (warp_dense) served the row
     } else if (need_mass) {
-      // dense path over the whole row (no usable survivor list)
+      // radix path over the whole row (no usable survivor list, or the dense path's
+      // crossing bin held too many candidates)
       status |= MTR_ROW_SLOW_PATH;
       u64 tot = 0;
 #pragma unroll 1
@@ -3625,6 +3887,8 @@ static int pick_kernel(const MtrSamplerArgs& a, const Derived& d, int sms) {
   if (a.vocab > WV_MAX && sk_supported(a, d)) return KERNEL_STREAM;
   if (a.vocab > WV_MAX || a.num_rows < 2 * (int64_t)sms) return KERNEL_ROW_CTA;
   if (d.pen_on && a.ids_len - a.penalty_start > WMAX_PEN_IDS) return KERNEL_ROW_CTA;
+  // top-p over the whole row stays on the row-per-CTA kernel: a warp's dense
+  // path (warp_dense) is latency-bound on a full row of exponentials
   const bool short_list = a.select_mode == MTR_SELECT_ARGMAX || (d.topk_on && a.top_k <= WARP_TOPK_MAX);
   return short_list ? KERNEL_ROW_WARP : KERNEL_ROW_CTA;
 }
