@@ -485,3 +485,22 @@ def test_append_and_stop_counts(cuda_device, workload):
     assert (got["id_buffer"][:, 39] == got["out_ids"]).all() and (got["id_buffer"][:, 17] == -1).all()
     ref, got = assert_parity(s.with_(cur_len_dev=np.array([40], dtype=np.int32)), cuda_device)
     assert (got["out_status"] & N.ROW_APPEND_SKIPPED).all() and (got["id_buffer"] == -1).all()
+
+
+@pytest.mark.parametrize("mode", [N.SELECT_SAMPLE, N.SELECT_NONE])
+def test_dense_mass_path_branches(cuda_device, mode):
+    # rows without a top-k list: Gaussian rows (the crossing bin lists < 64 candidates),
+    # a narrow score band (hundreds per 1/16-logit bin: the 256-sub-bin split) and
+    # exact ties (no split separates them: the radix path) -- on every kernel
+    rng = np.random.default_rng(71)
+    V, B = 4096, 96
+    x = rng.normal(0.0, 2.2, size=(B, V)).astype(np.float32)
+    x[1::3] = rng.uniform(0.0, 0.5, size=(len(x[1::3]), V)).astype(np.float32)
+    x[2::3] = 0.0
+    x[2::3, :10] = 1.0
+    s = W.StepInputs(logits=W.bf16_bits(x), dtype="bf16", num_rows=B, temperature=0.9, top_p=0.9, select_mode=mode,
+                     uniforms=rng.random(B, dtype=np.float32), want_scores=True, want_logprobs=True)
+    ref, got = assert_parity(s, cuda_device)
+    if _kernel["name"] == "warp":
+        slow = (got["out_status"] & N.ROW_SLOW_PATH) != 0
+        assert not slow[0::3].any() and not slow[1::3].any() and slow[2::3].all()
