@@ -195,6 +195,36 @@ class GrammarTable:
         return cls(torch.as_tensor(class_of, dtype=torch.uint8).to(device), allow.to(device))
 
 
+# Row status bits (include/mtr_sampler.h MTR_ROW_*): which ones mean the row's
+# token is not a draw from its scores.
+ROW_STATUS_NAMES = {N.ROW_NONFINITE: "nonfinite", N.ROW_ALL_MASKED: "all_masked", N.ROW_BAD_ID: "bad_id",
+                    N.ROW_BAD_UNIFORM: "bad_uniform", N.ROW_SLOW_PATH: "slow_path",
+                    N.ROW_TIE_AT_CUT: "tie_at_cut", N.ROW_COPY_TIMEOUT: "copy_timeout",
+                    N.ROW_APPEND_SKIPPED: "append_skipped"}
+PADDED_ROW_BITS = N.ROW_NONFINITE | N.ROW_ALL_MASKED | N.ROW_COPY_TIMEOUT
+
+
+def row_status_report(status, ids=None, pad_id: int | None = None) -> dict:
+    """Reads the per-row status words of a step: ``{name: [rows]}`` for every bit
+    that is set, plus ``"padded"`` — the rows whose token is ``pad_id`` because
+    the row could not be sampled (non-finite or fully masked scores, or a staged
+    copy that never landed: that row and every later row of its CTA).  ``status``
+    is a uint32 / int32 tensor or array of one word per row; with ``ids`` and
+    ``pad_id`` the report also checks that those rows carry ``pad_id``."""
+    import numpy as np
+
+    st = np.asarray(status.cpu() if hasattr(status, "cpu") else status).astype(np.int64) & 0xFFFFFFFF
+    rep = {name: np.nonzero(st & bit)[0].tolist() for bit, name in ROW_STATUS_NAMES.items() if (st & bit).any()}
+    padded = np.nonzero(st & PADDED_ROW_BITS)[0]
+    rep["padded"] = padded.tolist()
+    if ids is not None and pad_id is not None:
+        got = np.asarray(ids.cpu() if hasattr(ids, "cpu") else ids)
+        bad = [int(r) for r in padded if int(got[r]) != int(pad_id)]
+        if bad:
+            raise ValueError(f"rows {bad[:8]} are marked unsampleable but do not carry pad_id {pad_id}")
+    return rep
+
+
 class FusedSampler:
     """Stateful fused decode step for a fixed batch of ``num_rows`` rows.
 

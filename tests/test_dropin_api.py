@@ -452,3 +452,23 @@ def test_fused_sampler_graph_step_appends_and_stops(cuda_device):
     assert fs.all_finished() == eager.all_finished()
     assert int(cur.item()) == 2 + steps
     del graph
+
+
+def test_row_status_report_reads_the_contract():
+    # a hand-built step: row 1 non-finite, row 4 and every later row of its CTA lost
+    # their staged copy (header: MTR_ROW_COPY_TIMEOUT), row 2 a tie at the cut (info only)
+    status = np.zeros(8, dtype=np.uint32)
+    status[1] = N.ROW_NONFINITE
+    status[2] = N.ROW_TIE_AT_CUT
+    status[4] = N.ROW_COPY_TIMEOUT | N.ROW_SLOW_PATH
+    status[6] = N.ROW_COPY_TIMEOUT
+    ids = np.array([5, 7, 9, 11, 7, 13, 7, 2], dtype=np.int64)
+    rep = S.row_status_report(status, ids, pad_id=7)
+    assert rep["padded"] == [1, 4, 6]
+    assert rep["copy_timeout"] == [4, 6] and rep["tie_at_cut"] == [2] and rep["nonfinite"] == [1]
+    assert "bad_id" not in rep
+    ids[6] = 3  # a timed-out row that kept another token breaks the contract
+    with pytest.raises(ValueError):
+        S.row_status_report(status, ids, pad_id=7)
+    # int32 tensors (FusedSampler.status) read the same way
+    assert S.row_status_report(torch.from_numpy(status.view(np.int32)))["padded"] == [1, 4, 6]
