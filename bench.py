@@ -63,6 +63,9 @@ def parse_args():
     p.add_argument("--profile-workload", choices=["sharded", "b64", "lmhead", "v65536", "topp1024"], default="sharded")
     p.add_argument("--lm-steps", type=int, default=1024, help="steps per timed variant of the lm_head leg (0: skip)")
     p.add_argument("--sweep-steps", type=int, default=512, help="steps per sweep workload (0: skip)")
+    p.add_argument("--rows-curve", action="store_true",
+                   help="instead of the headline line: one line per pair count of the sharded step (16 .. 4096 "
+                        "CFG pairs, default kernel choice): how the step time follows the rows per GPU")
     p.add_argument("--sweep", action="store_true",
                    help="instead of the headline line: one line per vocabulary-sweep workload (rows x V bf16, "
                         "penalties + top_k 50 + top_p 0.95), device-timed, with its HBM roofline")
@@ -609,6 +612,54 @@ def run_reference(args, dist: Dist):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- step time against rows per GPU
+CURVE_PAIRS = (16, 64, 256, 512, 1024, 2048, 4096)
+
+
+def run_rows_curve(args, dist):
+    """`--rows-curve`: the sharded step (same chain as the headline) at each pair count of CURVE_PAIRS on
+    one GPU, graph-timed, logits rotating over > 3x L2.  Below one round of resident rows the step time
+    is the latency of one row, which is what bounds strong scaling across GPUs."""
+    from mapperatorinator_b200 import _native
+
+    _native.load()  # fail loudly without the native library
+    device = torch.device("cuda", dist.local)
+    torch.cuda.set_device(device)
+    stream = torch.cuda.Stream(device)
+    steps = max(64, min(args.steps, 1024))
+    peak, peak_kind = measured_peak()
+    for pairs in CURVE_PAIRS:
+        gen = torch.Generator(device).manual_seed(4321 + pairs)
+        sampler = sharded_sampler(device, pairs, gen)
+        history = torch.randint(0, VOCAB, (pairs, HISTORY), generator=gen, device=device)
+        nbuf = max(4, math.ceil(3 * L2_BYTES / (2 * pairs * VOCAB * 2)))
+        pool = [(torch.randn((2 * pairs, VOCAB), generator=gen, device=device) * 2.0).to(torch.bfloat16)
+                for _ in range(nbuf)]
+        upool = torch.rand((nbuf, pairs), generator=gen, device=device)
+
+        def step(i):
+            sampler.step(pool[i % nbuf], history, uniforms=upool[i % nbuf])
+
+        with torch.cuda.stream(stream):
+            for i in range(max(3, args.warmup)):
+                step(i)
+        torch.cuda.synchronize()
+        info = sampler.launch_info(pool[0], history, upool[0])
+        ms, graph = time_graph(step, steps, stream, dist)
+        ms = dist.max(ms)
+        del graph
+        us = ms * 1e3 / steps
+        gbs = algorithmic_bytes(pairs) / (us * 1e-6) / 1e9
+        if dist.rank == 0:
+            print(json.dumps({"workload": "rows_curve", "pairs": pairs, "us_per_step": round(us, 3),
+                              "tokens_per_s": pairs / (us * 1e-6), "achieved_gbs": round(gbs, 1),
+                              "frac": round(gbs / peak, 4), "peak_kind": peak_kind,
+                              "kernel": KERNEL_NAMES[info.kernel], "grid": info.grid, "threads": info.threads,
+                              "steps": steps}), flush=True)
+        del pool, upool, sampler, history
+        torch.cuda.empty_cache()
+
+
 # ---------------------------------------------------------------- vocabulary sweep
 SWEEP = ((256, 4096), (256, 16384), (256, 65536), (1024, 4096))
 
@@ -633,6 +684,8 @@ def main():
     try:
         if args.sweep:
             run_sweep(args, dist)
+        elif args.rows_curve:
+            run_rows_curve(args, dist)
         elif args.impl == "reference":
             run_reference(args, dist)
         else:
