@@ -478,6 +478,37 @@ __device__ __forceinline__ void sort64_desc(u64& a0, u64& a1, int lane) {
     a1 = t1;
   }
 }
+// Bitonic sort of 128 u64 keys held four per lane (positions 4*lane .. 4*lane+3),
+// descending; keys are distinct except the empty (zero) entries.  Stages whose
+// partner lies in another lane exchange by shuffle, the last two of every block
+// stay in registers.
+__device__ __forceinline__ void sort128_desc(u64 (&v)[4], int lane) {
+#pragma unroll
+  for (int k = 2; k <= 128; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j >= 1; j >>= 1) {
+      if (j >= 4) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const u64 p = __shfl_xor_sync(FULL, v[e], j >> 2);
+          const int P = 4 * lane + e;
+          const bool keep_larger = ((P & k) == 0) == ((P & j) == 0);
+          if ((p > v[e]) == keep_larger) v[e] = p;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if (e & j) continue;
+          const bool desc = ((4 * lane + e) & k) == 0;  // the lower position keeps the larger key
+          const u64 x = v[e], y = v[e | j];
+          const bool sw = desc ? (x < y) : (x > y);
+          v[e] = sw ? y : x;
+          v[e | j] = sw ? x : y;
+        }
+      }
+    }
+  }
+}
 // repetition (x < 0 ? x * rp : x / rp), then frequency and presence, each step
 // skipped when it is the identity (rp = 1, fp = 0, pp = 0); y = RN(1 / rp) or 0
 __device__ __forceinline__ float pen_value(float x, float c, float rp, float fp, float pp, float y) {

@@ -2864,7 +2864,8 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
     u64 qkept = 0;
     int32_t token = -1;
     int n = -1;  // survivors listed in lx / lid (-1: no list)
-    bool small = false;  // lx / lid hold the candidates (<= 64), not yet cut to the top k
+    bool small = false;  // mx / mi hold the candidates (<= 64), not yet cut to the top k
+    bool small128 = false;  // lx / lid hold 65 .. 128 candidates, not yet cut to the top k
 
     if (sel == MTR_SELECT_ARGMAX && !all_masked) {
       // lowest id of the maximum (of the first NaN when there is one)
@@ -3004,6 +3005,10 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
           if (total <= 64) {
             n = total;
             small = true;
+            topk_done = true;
+          } else if (total <= 128) {
+            n = total;
+            small128 = true;
             topk_done = true;
           } else if (total <= WCAP) {
             n = total;
@@ -3258,7 +3263,111 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
           token = __reduce_min_sync(FULL, my);
         }
       }
-    } else     if (need_mass && n >= 0) {
+    } else if (small128) {
+      // 65 .. 128 candidates: the same steps on one 128-key sort, four keys per lane
+      const uint32_t k = (uint32_t)a.top_k;
+      u64 kk[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = 4 * lane + e;
+        kk[e] = j < n ? (((u64)fkey(lx[j]) << 32) | (u64)(~(uint32_t)lid[j])) : 0ull;
+      }
+      sort128_desc(kk, lane);
+      auto key_at = [&](int pos) -> u64 {  // the key at sorted position pos (warp-uniform)
+        const int e = pos & 3;
+        const u64 x = e == 0 ? kk[0] : e == 1 ? kk[1] : e == 2 ? kk[2] : kk[3];
+        return __shfl_sync(FULL, x, pos >> 2);
+      };
+      const uint32_t tkey = (uint32_t)(key_at((int)k - 1) >> 32);
+      tk = key2f(tkey);
+      if (need_mass) {
+        uint32_t q[4];
+        expfx2(__fsub_rn(key2f((uint32_t)(kk[0] >> 32)), gmax), __fsub_rn(key2f((uint32_t)(kk[1] >> 32)), gmax), q[0],
+               q[1]);
+        expfx2(__fsub_rn(key2f((uint32_t)(kk[2] >> 32)), gmax), __fsub_rn(key2f((uint32_t)(kk[3] >> 32)), gmax), q[2],
+               q[3]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) q[e] = (kk[e] != 0ull && (uint32_t)(kk[e] >> 32) >= tkey) ? q[e] : 0u;
+        const u64 lsum = (u64)q[0] + q[1] + q[2] + q[3];
+        const u64 incl = warp_incl_scan_u64(lsum, lane);
+        qkept = __shfl_sync(FULL, incl, 31);
+        int pcut = 128;
+        if (dv.topp_on) {
+          const double P = __dmul_rn((double)a.top_p, (double)qkept);
+          const u64 plim = a.top_p_mode == MTR_TOPP_HF ? __double2ull_rz(ceil(P)) - 1ull : __double2ull_rz(floor(P));
+          u64 ab = incl - lsum;
+          int my = -1;
+          u64 myq = 0;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if (my < 0 && q[e] != 0u && ab <= plim && ab + q[e] > plim) {
+              my = 4 * lane + e;
+              myq = ab + q[e];
+            }
+            ab += q[e];
+          }
+          const unsigned bal = __ballot_sync(FULL, my >= 0);
+          const int src = max(__ffs(bal) - 1, 0);
+          pcut = max(__shfl_sync(FULL, my, src), 0);
+          qkept = __shfl_sync(FULL, myq, src);
+          const u64 ck = key_at(pcut), nk = key_at(min(pcut + 1, 127));
+          cut_x = key2f((uint32_t)(ck >> 32));
+          cut_id = (int32_t)(~(uint32_t)ck);
+          topp_cut = true;
+          if (pcut + 1 < 128 && nk != 0ull && (uint32_t)(nk >> 32) == (uint32_t)(ck >> 32)) status |= MTR_ROW_TIE_AT_CUT;
+        }
+        if (sel == MTR_SELECT_SAMPLE) {
+          // the draw through 32 id buckets, as on the 64-key list
+          const u64 R = __double2ull_rz(floor(__dmul_rn((double)u, (double)qkept)));
+          bool kp[4];
+          int ii[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            kp[e] = q[e] != 0u && 4 * lane + e <= pcut;
+            ii[e] = (int)(~(uint32_t)kk[e]);
+          }
+          int bsh = 3;
+          while ((32 << bsh) < VP) ++bsh;
+          uint32_t* const bk = hc;
+          *(uint2*)(bk + 2 * lane) = make_uint2(0u, 0u);
+          __syncwarp();
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (kp[e]) {
+              atomicAdd(bk + 2 * (ii[e] >> bsh), q[e] & 0xffffu);
+              atomicAdd(bk + 2 * (ii[e] >> bsh) + 1, q[e] >> 16);
+            }
+          __syncwarp();
+          const uint2 hh = *(const uint2*)(bk + 2 * lane);
+          const u64 hb = ((u64)hh.y << 16) + hh.x;
+          const u64 incl2 = warp_incl_scan_u64(hb, lane);
+          const int b = max(__ffs(__ballot_sync(FULL, incl2 > R)) - 1, 0);
+          const u64 f0 = __shfl_sync(FULL, incl2 - hb, b);
+          u64 f[4] = {f0, f0, f0, f0};
+          bool in[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) in[e] = kp[e] && (ii[e] >> bsh) == b;
+#pragma unroll
+          for (int e0 = 0; e0 < 4; ++e0) {
+            unsigned mm = __ballot_sync(FULL, in[e0]);
+#pragma unroll 1
+            while (mm) {  // each entry of the bucket adds its mass to the entries at or above its id
+              const int src = __ffs(mm) - 1;
+              mm &= mm - 1u;
+              const int is = __shfl_sync(FULL, ii[e0], src);
+              const uint32_t qs = __shfl_sync(FULL, q[e0], src);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) f[e] += is <= ii[e] ? qs : 0u;
+            }
+          }
+          int32_t my = NO_ID;
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (in[e] && f[e] > R && f[e] - q[e] <= R) my = min(my, ii[e]);
+          token = __reduce_min_sync(FULL, my);
+        }
+      }
+    } else if (need_mass && n >= 0) {
       // on the survivor list
 #pragma unroll 1
       for (int j = lane; j < n; j += 32) lq[j] = expfx(__fsub_rn(lx[j], gmax));

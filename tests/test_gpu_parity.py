@@ -504,3 +504,19 @@ def test_dense_mass_path_branches(cuda_device, mode):
     if _kernel["name"] == "warp":
         slow = (got["out_status"] & N.ROW_SLOW_PATH) != 0
         assert not slow[0::3].any() and not slow[1::3].any() and slow[2::3].all()
+
+
+@pytest.mark.parametrize("top_k,top_p,mode,scores", [(50, 0.9, N.TOPP_HF, False), (100, 0.95, N.TOPP_SAMPLE_FN, True),
+                                                     (100, 1.0, N.TOPP_HF, False), (64, 0.5, N.TOPP_HF, True)])
+def test_quantized_scores_long_candidate_lists(cuda_device, top_k, top_p, mode, scores):
+    # scores on a 1/4-logit grid: the tie group at the k-th score makes the
+    # candidate list 65 .. 128 long in most rows (the row-per-warp kernel's
+    # 128-key sort) and longer in some (its fine-bin list path)
+    rng = np.random.default_rng(81 + top_k)
+    B, V, L = 256, 4096, 256
+    x = (np.round(rng.normal(0.0, 2.0, size=(B, V)) * 4.0) / 4.0).astype(np.float32)
+    s = W.StepInputs(logits=W.bf16_bits(x), dtype="bf16", num_rows=B, select_mode=N.SELECT_SAMPLE, top_k=top_k,
+                     top_p=top_p, top_p_mode=mode, uniforms=rng.random(B, dtype=np.float32), want_scores=scores,
+                     input_ids=rng.integers(0, V, size=(B, L)).astype(np.int64), repetition_penalty=1.25,
+                     presence_penalty=0.25)
+    assert_parity(s, cuda_device)
