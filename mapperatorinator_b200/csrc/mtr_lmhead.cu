@@ -162,6 +162,11 @@ __global__ void __launch_bounds__(128, 1)
   const int KB = p.kblocks;
   const int first = KB < S ? KB : S;
   if (threadIdx.x == 0) {
+    // the descriptors first, then the barriers; launched as a programmatic
+    // dependent, the CTA reaches here while the previous kernel drains, and
+    // waits for it (griddepcontrol.wait) before its first global access
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_h) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&map_w) : "memory");
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -170,6 +175,7 @@ __global__ void __launch_bounds__(128, 1)
     abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    wait_prior_grid();
     for (int kb = 0; kb < first; ++kb) {
       mbar_expect_tx(&full[kb], RG::STAGE_BYTES);
       tma_load_2d(a_tile(kb), &map_h, kb * BK, m0, &full[kb]);
@@ -185,6 +191,7 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  wait_prior_grid();  // every thread: its logits stores follow the previous kernel's reads
   const uint32_t tmem = tmem_slot;
 
   if (warp == 0 && lane == 0) {
@@ -338,8 +345,16 @@ static cudaError_t launch_bn(const MtrLmHeadArgs& a, cudaStream_t s) {
   p.kblocks = a.d_model / BK;
   p.err = a.error_word;
   const dim3 grid((unsigned)((a.vocab + BN - 1) / BN), (unsigned)((a.rows + BM - 1) / BM), 1);
-  kern<<<grid, 128, Ring<BN>::BYTES, s>>>(mh, mw, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = Ring<BN>::BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  cfg.numAttrs = launch_attrs(attr, 1, true);
+  cfg.attrs = attr;
+  return cudaLaunchKernelEx(&cfg, kern, mh, mw, p);
 }
 
 }  // namespace lm
