@@ -30,7 +30,10 @@
 // row of tensor memory holds at most 512 fp32 columns, so the logits of one step
 // meet the sampler in L2 (R x V x 2 bytes, 2 MiB for 256 x 4096): the sampler
 // launch that follows uses programmatic dependent launch and waits for this
-// grid at griddepcontrol.wait.
+// grid at griddepcontrol.wait.  This kernel lets its dependents in only as its
+// CTAs exit (no early launch_dependents): admitted during the epilogue, the
+// sampler's CTAs crowded onto the few SMs without a 150 KB projection CTA and
+// the pair took 1.9 us longer.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -241,7 +244,6 @@ __global__ void __launch_bounds__(128, 1)
   bool waited = true;
   if (lane == 0) waited = mbar_wait(&done, 0, WAIT_NS);
   waited = __shfl_sync(FULL, waited, 0) != 0;
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   tc_fence_after();
   // tcgen05.ld is warp-collective: the whole warp reads or none of it
   const bool go = __all_sync(FULL, waited && !abort_flag);
