@@ -104,12 +104,12 @@ static SkGeo sk_geo(const MtrSamplerArgs& a, const Derived& d, int sms) {
   return g;
 }
 
-static const void* stream_kernel_for(const MtrSamplerArgs& a, int shape) {
+static const void* stream_kernel_for(const MtrSamplerArgs& a, int shape, bool j4) {
   const bool cfg = a.cfg_enabled != 0;
   switch (a.logits_dtype) {
-    case MTR_DTYPE_F32: return stream_kernel_f32(cfg, shape);
-    case MTR_DTYPE_BF16: return stream_kernel_bf16(cfg, shape);
-    default: return stream_kernel_f16(cfg, shape);
+    case MTR_DTYPE_F32: return stream_kernel_f32(cfg, shape, j4);
+    case MTR_DTYPE_BF16: return stream_kernel_bf16(cfg, shape, j4);
+    default: return stream_kernel_f16(cfg, shape, j4);
   }
 }
 
@@ -120,21 +120,22 @@ static cudaError_t sk_shape(const MtrSamplerArgs& a, const SkGeo& g, int sms, Sk
   out->threads = g.R * g.G * 32;
   out->shape = out->threads <= 128 ? SK_SHAPE_128 : out->threads <= 256 ? SK_SHAPE_256 : SK_SHAPE_512;
   out->dyn = SK_LUT_BYTES + g.R * g.group_bytes;
-  const void* kern = stream_kernel_for(a, out->shape);
+  out->j4 = (int64_t)4 * 256 * g.G >= (int64_t)a.vocab;
+  const void* kern = stream_kernel_for(a, out->shape, out->j4 != 0);
   {
     static std::mutex mu;
-    static const void* done[64][18];
+    static const void* done[64][36];
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
     std::lock_guard<std::mutex> lk(mu);
     bool set = false;
-    for (int i = 0; i < 18; ++i) set |= done[dev][i] == kern;
+    for (int i = 0; i < 36; ++i) set |= done[dev][i] == kern;
     if (!set) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
       if (e != cudaSuccess) return e;
-      for (int i = 0; i < 18; ++i)
+      for (int i = 0; i < 36; ++i)
         if (!done[dev][i]) {
           done[dev][i] = kern;
           break;
@@ -152,7 +153,7 @@ static cudaError_t sk_shape(const MtrSamplerArgs& a, const SkGeo& g, int sms, Sk
 
 cudaError_t stream_launch(const MtrSamplerArgs& a, const Derived& d, int sms, cudaStream_t s) {
   const SkGeo g = sk_geo(a, d, sms);
-  SkLaunch sh;
+  SkLaunch sh{};
   const cudaError_t e = sk_shape(a, g, sms, &sh);
   if (e != cudaSuccess) return e;
   switch (a.logits_dtype) {
@@ -164,7 +165,7 @@ cudaError_t stream_launch(const MtrSamplerArgs& a, const Derived& d, int sms, cu
 
 void stream_query(const MtrSamplerArgs& a, const Derived& d, int sms, MtrLaunchInfo* out) {
   const SkGeo g = sk_geo(a, d, sms);
-  SkLaunch sh;
+  SkLaunch sh{};
   if (sk_shape(a, g, sms, &sh) != cudaSuccess) {
     cudaGetLastError();  // no device: report the launch bound (28 warps per SM)
     sh.threads = g.R * g.G * 32;
@@ -174,7 +175,7 @@ void stream_query(const MtrSamplerArgs& a, const Derived& d, int sms, MtrLaunchI
     sh.grid = (int)(ctas < cap ? ctas : cap);
   }
   out->threads = sh.threads;
-  out->elems_per_thread = 8 * SK_J;
+  out->elems_per_thread = 8 * (sh.j4 ? 4 : SK_J);
   out->cluster_size = 1;
   out->grid = sh.grid;
   out->dyn_smem_bytes = sh.dyn;

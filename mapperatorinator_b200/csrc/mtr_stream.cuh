@@ -90,6 +90,7 @@ struct SkGeo {
 
 struct SkLaunch {
   int threads, dyn, grid, shape;
+  int j4;  // the 4-slot instantiation (4 * 256 * G >= V)
 };
 
 struct alignas(16) SkHead {
@@ -959,7 +960,9 @@ __device__ __noinline__ void sk_walk(const SkRow<Tin, CFG> r, const MtrSamplerAr
   g.sync();
 }
 
-template <typename Tin, bool CFG, int MAXT, int MINB>
+// J: 8-id chunk slots per thread (4 or SK_J); the host picks J = 4 when
+// 4 * 256 * G >= V, so no slot array is sized beyond what the row needs.
+template <typename Tin, bool CFG, int MAXT, int MINB, int J>
 __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constant__ MtrSamplerArgs a,
                                                           const __grid_constant__ Derived dv,
                                                           const __grid_constant__ SkGeo geo) {
@@ -1047,8 +1050,9 @@ __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constan
         l2_prefetch(r.idsr + (size_t)h0 * ids_esz, (size_t)(L - h0) * ids_esz);
       }
     }
-    uint4 bufA[2][NV], bufB[2][NV];
-    if (gt < nch) r.ld_chunk(gt, bufA[0], bufB[0]);
+    constexpr int NBUF = J <= 4 ? J : 2;  // J <= 4: every chunk of the row in flight at once
+    uint4 bufA[NBUF][NV], bufB[NBUF][NV];
+    if (J > 4 && gt < nch) r.ld_chunk(gt, bufA[0], bufB[0]);
 
     // ---------------- per-row scalars (every thread, the same addresses)
     uint32_t st = 0;
@@ -1205,13 +1209,18 @@ __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constan
     // A NaN, infinite or huge bound marks the chunk special: it is always read
     // again exactly (which finds the non-finite scores) and never binned.
     const bool approx = sizeof(Tin) == 2 && !r.bias_on && (!CFG || geo.bound_cfg);
-    float ub[SK_J];
+    float ub[J];
     float wmax = 0.0f, rmax = NEG;
+    if constexpr (J <= 4) {
 #pragma unroll
-    for (int j = 0; j < SK_J; ++j) {
+      for (int j = 0; j < J; ++j)
+        if (j * GT + gt < nch) r.ld_chunk(j * GT + gt, bufA[j], bufB[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
       const int c = j * GT + gt;
-      const int s = j & 1;
-      if (j + 1 < SK_J && c + GT < nch) r.ld_chunk(c + GT, bufA[s ^ 1], bufB[s ^ 1]);
+      const int s = J <= 4 ? j : (j & 1);
+      if (J > 4 && j + 1 < J && c + GT < nch) r.ld_chunk(c + GT, bufA[s ^ 1], bufB[s ^ 1]);
       float m = NEG;
       const uint32_t keep = c < nch ? r.keep_of(c, true) : 0u;
       if (__any_sync(FULL, keep != 0u)) {
@@ -1253,7 +1262,7 @@ __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constan
 #pragma unroll 1
       for (int lvl = 0; lvl < 2; ++lvl) {
 #pragma unroll
-        for (int j = 0; j < SK_J; ++j) {
+        for (int j = 0; j < J; ++j) {
           if (ub[j] > NEG && ub[j] < pos_inf()) {
             // bin of the chunk's lower bound lb = RD(ub - W2) (<= its largest score):
             // bin <= b* implies Ms - lb < (b* + 1) / scale, i.e. lb > T
@@ -1296,7 +1305,7 @@ __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constan
       // ---------------- listing: chunks whose maximum reaches the bound
       uint32_t qm = 0;
 #pragma unroll
-      for (int j = 0; j < SK_J; ++j)
+      for (int j = 0; j < J; ++j)
         if (ub[j] > NEG && ub[j] >= lower) qm |= 1u << j;  // special chunks (+inf) always
       const uint32_t nqt = __popc(qm);
       const uint32_t qincl = warp_incl_scan_u32(nqt, lane);
@@ -1349,7 +1358,7 @@ __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constan
         }
       } else {
 #pragma unroll 1
-        for (int j = 0; j < SK_J; ++j) list_chunk(j * GT + gt, ((qm >> j) & 1u) != 0u);
+        for (int j = 0; j < J; ++j) list_chunk(j * GT + gt, ((qm >> j) & 1u) != 0u);
       }
 
       // ---------------- history ids: penalised scores
@@ -1480,9 +1489,9 @@ __global__ void __launch_bounds__(MAXT, MINB) stream_kernel(const __grid_constan
 
 // Per element type (mtr_stream_{bf16,f16,f32}.cu): the kernel of (cfg, shape)
 // and its launch.
-const void* stream_kernel_bf16(bool cfg, int shape);
-const void* stream_kernel_f16(bool cfg, int shape);
-const void* stream_kernel_f32(bool cfg, int shape);
+const void* stream_kernel_bf16(bool cfg, int shape, bool j4);
+const void* stream_kernel_f16(bool cfg, int shape, bool j4);
+const void* stream_kernel_f32(bool cfg, int shape, bool j4);
 cudaError_t stream_launch_bf16(const MtrSamplerArgs& a, const Derived& d, const SkGeo& g, const SkLaunch& sh,
                                cudaStream_t s);
 cudaError_t stream_launch_f16(const MtrSamplerArgs& a, const Derived& d, const SkGeo& g, const SkLaunch& sh,
@@ -1492,13 +1501,16 @@ cudaError_t stream_launch_f32(const MtrSamplerArgs& a, const Derived& d, const S
 
 // The instantiations of one element type: shapes 128 (7 CTAs / SM), 256 (3) and
 // 512 (2 CTAs / SM) threads.
+#define MTR_STREAM_KERNEL(TIN, C, SHAPE, J4)                                                                    \
+  ((SHAPE) == SK_SHAPE_128 ? ((J4) ? (const void*)stream_kernel<TIN, C, 128, 7, 4>                              \
+                                   : (const void*)stream_kernel<TIN, C, 128, 7, SK_J>)                          \
+   : (SHAPE) == SK_SHAPE_256 ? ((J4) ? (const void*)stream_kernel<TIN, C, 256, 3, 4>                            \
+                                     : (const void*)stream_kernel<TIN, C, 256, 3, SK_J>)                        \
+   : ((J4) ? (const void*)stream_kernel<TIN, C, 512, 2, 4> : (const void*)stream_kernel<TIN, C, 512, 2, SK_J>))
+
 #define MTR_STREAM_INSTANTIATE(TIN, NAME)                                                                        \
-  const void* stream_kernel_##NAME(bool cfg, int shape) {                                                       \
-    if (shape == SK_SHAPE_128) return cfg ? (const void*)stream_kernel<TIN, true, 128, 7>                        \
-                                          : (const void*)stream_kernel<TIN, false, 128, 7>;                      \
-    if (shape == SK_SHAPE_256) return cfg ? (const void*)stream_kernel<TIN, true, 256, 3>                        \
-                                          : (const void*)stream_kernel<TIN, false, 256, 3>;                      \
-    return cfg ? (const void*)stream_kernel<TIN, true, 512, 2> : (const void*)stream_kernel<TIN, false, 512, 2>; \
+  const void* stream_kernel_##NAME(bool cfg, int shape, bool j4) {                                              \
+    return cfg ? MTR_STREAM_KERNEL(TIN, true, shape, j4) : MTR_STREAM_KERNEL(TIN, false, shape, j4);            \
   }                                                                                                               \
   cudaError_t stream_launch_##NAME(const MtrSamplerArgs& a, const Derived& d, const SkGeo& g, const SkLaunch& sh, \
                                    cudaStream_t s) {                                                             \
@@ -1511,15 +1523,9 @@ cudaError_t stream_launch_f32(const MtrSamplerArgs& a, const Derived& d, const S
     cudaLaunchAttribute attr[2];                                                                                  \
     cfg.numAttrs = launch_attrs(attr, 1, d.pdl != 0);                                                             \
     cfg.attrs = cfg.numAttrs ? attr : nullptr;                                                                    \
-    const bool c = a.cfg_enabled != 0;                                                                            \
-    if (sh.shape == SK_SHAPE_128)                                                                                 \
-      return c ? cudaLaunchKernelEx(&cfg, stream_kernel<TIN, true, 128, 7>, a, d, g)                             \
-               : cudaLaunchKernelEx(&cfg, stream_kernel<TIN, false, 128, 7>, a, d, g);                           \
-    if (sh.shape == SK_SHAPE_256)                                                                                 \
-      return c ? cudaLaunchKernelEx(&cfg, stream_kernel<TIN, true, 256, 3>, a, d, g)                             \
-               : cudaLaunchKernelEx(&cfg, stream_kernel<TIN, false, 256, 3>, a, d, g);                           \
-    return c ? cudaLaunchKernelEx(&cfg, stream_kernel<TIN, true, 512, 2>, a, d, g)                               \
-             : cudaLaunchKernelEx(&cfg, stream_kernel<TIN, false, 512, 2>, a, d, g);                             \
+    const void* kern = stream_kernel_##NAME(a.cfg_enabled != 0, sh.shape, sh.j4 != 0);                           \
+    void* params[3] = {(void*)&a, (void*)&d, (void*)&g};                                                         \
+    return cudaLaunchKernelExC(&cfg, kern, params);                                                               \
   }
 
 }  // namespace mtr
