@@ -326,11 +326,12 @@ __device__ __forceinline__ void collect(Shared<CS>& sm, uint32_t mask, const flo
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// Residency: three CTAs per SM for one 256-thread CTA per row (80 registers,
-// no spills; the many-row top-p case runs 15 % faster than at two), two for the
+// Residency: four CTAs per SM for one 256-thread CTA per row (64 registers, a
+// few spilled; 1024 top-p-only rows run 9 % faster than at three, 25 % faster
+// than at two; with the penalty tiles in shared memory three fit), two for the
 // 256-thread clusters (which would spill at three), one for the wider CTAs.
 template <typename Tin, int THREADS, int EPT, int CS>
-__global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? (CS == 1 ? 3 : 2) : 1))
+__global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? (CS == 1 ? 4 : 2) : 1))
     sampler_kernel(const __grid_constant__ MtrSamplerArgs a, const __grid_constant__ Derived dv) {
   wait_prior_grid();
   allow_dependents();
