@@ -326,12 +326,14 @@ __device__ __forceinline__ void collect(Shared<CS>& sm, uint32_t mask, const flo
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-// Residency: four CTAs per SM for one 256-thread CTA per row (64 registers, a
-// few spilled; 1024 top-p-only rows run 9 % faster than at three, 25 % faster
-// than at two; with the penalty tiles in shared memory three fit), two for the
-// 256-thread clusters (which would spill at three), one for the wider CTAs.
-template <typename Tin, int THREADS, int EPT, int CS>
-__global__ void __launch_bounds__(THREADS, (THREADS <= 256 ? (CS == 1 ? 4 : 2) : 1))
+// Residency (MINB): three CTAs per SM for one 256-thread CTA per row (80
+// registers, no spills), four in the instantiation for launches of more rows
+// than one round of three holds (64 registers, a few spilled: 1024 top-p-only
+// rows run 9 % faster than at three, but rows that fit one round run up to 19 %
+// slower, so they keep three), two for the 256-thread clusters (which would
+// spill at three), one for the wider CTAs.
+template <typename Tin, int THREADS, int EPT, int CS, int MINB = (THREADS <= 256 ? (CS == 1 ? 3 : 2) : 1)>
+__global__ void __launch_bounds__(THREADS, MINB)
     sampler_kernel(const __grid_constant__ MtrSamplerArgs a, const __grid_constant__ Derived dv) {
   wait_prior_grid();
   allow_dependents();
@@ -3725,6 +3727,7 @@ __global__ void __launch_bounds__(32, 10) row_warp_kernel(const __grid_constant_
 // ---------------------------------------------------------------------------
 struct Geo {
   int threads, ept, cs;
+  int wide = 0;  // 256-thread CTAs, four per SM (more rows than one round of three holds)
 };
 
 // Up to one row per SM of a small vocabulary: one 512-thread CTA per row (8 ids
@@ -3733,7 +3736,7 @@ struct Geo {
 static Geo pick_geo(int V, int64_t B, int sms) {
   if (V <= 4096) {
     if (B <= sms) return {512, 8, 1};
-    return {256, 16, 1};
+    return {256, 16, 1, B > 3 * (int64_t)sms ? 1 : 0};
   }
   if (V <= 8192) return {256, 16, 2};
   if (V <= 16384) return {256, 16, 4};
@@ -3926,9 +3929,9 @@ static Derived derive(const MtrSamplerArgs& a) {
   return d;
 }
 
-template <typename Tin, int TH, int EPT, int CS>
+template <typename Tin, int TH, int EPT, int CS, int MINB = (TH <= 256 ? (CS == 1 ? 3 : 2) : 1)>
 static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, cudaStream_t s) {
-  auto kern = sampler_kernel<Tin, TH, EPT, CS>;
+  auto kern = sampler_kernel<Tin, TH, EPT, CS, MINB>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   int dev = 0;
@@ -3988,10 +3991,33 @@ cudaError_t cached_occupancy(const void* kern, int threads, int dyn, int* occ) {
 // streaming row-group kernel (several warps per row, no staged row: 2-8x the
 // row-per-CTA kernel there).  For V <= 4096 the row-per-warp kernel wins when
 // many rows each end in a short list (argmax, or top-k with k <=
-// WARP_TOPK_MAX).  Everything else (top-p over the whole row, column
-// temperatures, few rows) takes the row-per-CTA kernel.  The flags force a kernel.
+// WARP_TOPK_MAX) and more rows than one round of row-per-CTA CTAs holds.
+// Everything else (top-p over the whole row, column temperatures, rows that fit
+// one round of CTAs) takes the row-per-CTA kernel.  The flags force a kernel.
 constexpr int WARP_TOPK_MAX = 128;
 enum { KERNEL_ROW_CTA = 0, KERNEL_ROW_WARP = 1, KERNEL_STREAM = 2 };
+
+template <typename Tin>
+static const void* cta256_ptr() {
+  return (const void*)sampler_kernel<Tin, 256, 16, 1>;
+}
+// Rows that one round of row-per-CTA CTAs holds at a V <= 4096 launch (one
+// 512-thread CTA per SM up to #SMs rows, else the 256-thread CTAs' occupancy:
+// 3 per SM, penalty tiles included).  Within one round the row-per-CTA kernel beats the row-per-warp
+// kernel (sharded chain, 296-440 pairs: 14.1-14.5 us against 15.6-16.0).
+static int64_t cta_round_rows(const MtrSamplerArgs& a, const Derived& d, int sms) {
+  if (a.num_rows <= sms) return sms;
+  const Geo g = pick_geo(a.vocab, a.num_rows, sms);
+  const void* k = a.logits_dtype == MTR_DTYPE_F32    ? cta256_ptr<float>()
+                  : a.logits_dtype == MTR_DTYPE_BF16 ? cta256_ptr<__nv_bfloat16>()
+                                                     : cta256_ptr<__half>();
+  int occ = 0;
+  if (cached_occupancy(k, g.threads, dyn_smem_bytes(g, d.pen_on != 0), &occ) != cudaSuccess) {
+    cudaGetLastError();
+    occ = 3;  // no device: the launch bound
+  }
+  return (int64_t)occ * sms;
+}
 
 static int pick_kernel(const MtrSamplerArgs& a, const Derived& d, int sms) {
   if (a.flags & MTR_FLAG_KERNEL_ROW_CTA) return KERNEL_ROW_CTA;
@@ -3999,7 +4025,7 @@ static int pick_kernel(const MtrSamplerArgs& a, const Derived& d, int sms) {
   if (a.flags & MTR_FLAG_KERNEL_STREAM) return KERNEL_STREAM;
   if (a.lookback_mode != MTR_LOOKBACK_OFF) return KERNEL_ROW_CTA;  // the lookback bias lives in the row-per-CTA kernel
   if (a.vocab > WV_MAX && sk_supported(a, d)) return KERNEL_STREAM;
-  if (a.vocab > WV_MAX || a.num_rows < 2 * (int64_t)sms) return KERNEL_ROW_CTA;
+  if (a.vocab > WV_MAX || a.num_rows <= cta_round_rows(a, d, sms)) return KERNEL_ROW_CTA;
   if (d.pen_on && a.ids_len - a.penalty_start > WMAX_PEN_IDS) return KERNEL_ROW_CTA;
   // top-p over the whole row stays on the row-per-CTA kernel: a warp's dense
   // path (warp_dense) is latency-bound on a full row of exponentials
@@ -4058,7 +4084,8 @@ static cudaError_t launch_warp(const MtrSamplerArgs& a, const Derived& d, cudaSt
 template <typename Tin>
 static cudaError_t launch_dtype(const MtrSamplerArgs& a, const Derived& d, const Geo& g, int dyn, cudaStream_t s) {
   if (g.threads == 512 && g.ept == 8 && g.cs == 1) return launch_t<Tin, 512, 8, 1>(a, d, dyn, s);
-  if (g.threads == 256 && g.cs == 1) return launch_t<Tin, 256, 16, 1>(a, d, dyn, s);
+  if (g.threads == 256 && g.cs == 1)
+    return g.wide ? launch_t<Tin, 256, 16, 1, 4>(a, d, dyn, s) : launch_t<Tin, 256, 16, 1>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 2) return launch_t<Tin, 256, 16, 2>(a, d, dyn, s);
   if (g.threads == 256 && g.cs == 4) return launch_t<Tin, 256, 16, 4>(a, d, dyn, s);
   if (g.threads == 512 && g.cs == 4) return launch_t<Tin, 512, 16, 4>(a, d, dyn, s);
