@@ -3929,9 +3929,11 @@ static Derived derive(const MtrSamplerArgs& a) {
   return d;
 }
 
+// The row-per-CTA kernel's opt-in to large dynamic shared memory, once per
+// device and instantiation; it must precede any occupancy query of a launch
+// whose shared memory passes 48 KB (the query reports 0 CTAs without it).
 template <typename Tin, int TH, int EPT, int CS, int MINB = (TH <= 256 ? (CS == 1 ? 3 : 2) : 1)>
-static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, cudaStream_t s) {
-  auto kern = sampler_kernel<Tin, TH, EPT, CS, MINB>;
+static cudaError_t cta_attr() {
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   int dev = 0;
@@ -3940,9 +3942,17 @@ static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, 
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   std::call_once(once[dev], [&]() {
     const int max_dyn = 227 * 1024 - (int)sizeof(Shared<CS>);
-    attr_err[dev] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn);
+    attr_err[dev] = cudaFuncSetAttribute(sampler_kernel<Tin, TH, EPT, CS, MINB>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn);
   });
-  if (attr_err[dev] != cudaSuccess) return attr_err[dev];
+  return attr_err[dev];
+}
+
+template <typename Tin, int TH, int EPT, int CS, int MINB = (TH <= 256 ? (CS == 1 ? 3 : 2) : 1)>
+static cudaError_t launch_t(const MtrSamplerArgs& a, const Derived& d, int dyn, cudaStream_t s) {
+  auto kern = sampler_kernel<Tin, TH, EPT, CS, MINB>;
+  const cudaError_t ae = cta_attr<Tin, TH, EPT, CS, MINB>();
+  if (ae != cudaSuccess) return ae;
   cudaLaunchConfig_t cfg;
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)(a.num_rows * CS), 1, 1);
@@ -3999,6 +4009,7 @@ enum { KERNEL_ROW_CTA = 0, KERNEL_ROW_WARP = 1, KERNEL_STREAM = 2 };
 
 template <typename Tin>
 static const void* cta256_ptr() {
+  if (cta_attr<Tin, 256, 16, 1>() != cudaSuccess) return nullptr;
   return (const void*)sampler_kernel<Tin, 256, 16, 1>;
 }
 // Rows that one round of row-per-CTA CTAs holds at a V <= 4096 launch (one
@@ -4012,7 +4023,7 @@ static int64_t cta_round_rows(const MtrSamplerArgs& a, const Derived& d, int sms
                   : a.logits_dtype == MTR_DTYPE_BF16 ? cta256_ptr<__nv_bfloat16>()
                                                      : cta256_ptr<__half>();
   int occ = 0;
-  if (cached_occupancy(k, g.threads, dyn_smem_bytes(g, d.pen_on != 0), &occ) != cudaSuccess) {
+  if (!k || cached_occupancy(k, g.threads, dyn_smem_bytes(g, d.pen_on != 0), &occ) != cudaSuccess) {
     cudaGetLastError();
     occ = 3;  // no device: the launch bound
   }
