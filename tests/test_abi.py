@@ -145,6 +145,8 @@ def test_query_geometry(lib, vocab, rows, cs):
 @pytest.mark.parametrize("rows,vocab,top_k,select,flags,kernel", [
     (4096, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_WARP),      # many rows, short top-k list
     (64, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),         # few rows: latency geometry
+    (444, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_CTA),        # one round of CTAs (3 per SM x 148)
+    (445, 4096, 50, N.SELECT_SAMPLE, 0, N.KERNEL_ROW_WARP),       # past one round: row per warp
     (256, 65536, 50, N.SELECT_SAMPLE, 0, N.KERNEL_STREAM),        # large vocabulary: 16 warps per row
     (256, 16384, 50, N.SELECT_NONE, 0, N.KERNEL_STREAM),          # processor output with top-k
     (4096, 8192, 50, N.SELECT_SAMPLE, 0, N.KERNEL_STREAM),
