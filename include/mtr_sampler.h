@@ -317,9 +317,10 @@ int mtr_sampler_query(int32_t vocab, int32_t num_rows, int32_t with_penalties, M
 /* Kernel and geometry mtr_sampler_launch would use for these exact arguments
  * (validates them first).  Without a kernel flag the streaming row-group
  * kernel is chosen whenever it serves the request (see MTR_FLAG_KERNEL_STREAM);
- * otherwise the row-per-warp kernel for >= 2 rows per SM of a vocabulary
- * <= 4096 whose selection is argmax or a top-k <= 128, else the row-per-CTA
- * kernel.  A kernel flag the request does not fit returns MTR_ERR_UNSUPPORTED. */
+ * otherwise the row-per-warp kernel for more rows than one round of
+ * row-per-CTA CTAs holds (3 per SM) of a vocabulary <= 4096 whose selection
+ * is argmax or a top-k <= 128, else the row-per-CTA kernel.  A kernel flag the
+ * request does not fit returns MTR_ERR_UNSUPPORTED. */
 int mtr_sampler_query_args(const MtrSamplerArgs* args, MtrLaunchInfo* out);
 
 /*
